@@ -1,0 +1,158 @@
+// decode_bulk.cu -- "bulk" kernel family: persistent CTAs (one per SM) that
+// stream contiguous runs of units through a shared-memory ring with 1-D
+// cp.async.bulk copies completing on mbarriers, consumed by 8 compute warps.
+//
+// Per CTA: warp 0 lane 0 is the producer; warps 1..8 are consumers. The CTA
+// owns chunks c = blockIdx.x + k*gridDim.x (k = 0, 1, ...); chunk c covers
+// units [c*CU, min((c+1)*CU, units)), i.e. three contiguous byte ranges (K
+// slabs, V slabs, Q rows), each moved by one bulk copy into ring stage
+// k % NS. A chunk holds CT tiles; consumer warp w takes flat jobs
+// f = w, w+8, ... (chunk f / CT, tile f % CT), waits for the stage's `full`
+// phase, computes the tile from shared memory, arrives on the stage's `empty`
+// barrier (count CT) and streams its fp16 output rows straight to global.
+//
+// Compiled once per head_dim: -DFMHA_HEAD_DIM=128 or 256.
+#include "decode_common.cuh"
+
+#ifndef FMHA_HEAD_DIM
+#error "compile with -DFMHA_HEAD_DIM=128 or 256"
+#endif
+
+namespace fmha {
+
+template <int D, int SMAX, int G>
+__global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Params P) {
+  using T = TileShape<D, SMAX, G>;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ncw = (blockDim.x >> 5) - 1;  // consumer warps
+  const int NS = P.stages;
+  const uint32_t full0 = smem_u32(smem);
+  const uint32_t empty0 = full0 + 8u * NS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * NS);
+  const uint32_t ring0 = smem_u32(smem + P.ring_off);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(full0 + 8u * i, 1);
+      mbar_init(empty0 + 8u * i, P.tiles_per_chunk);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  const int my_chunks =
+      P.chunks > (int)blockIdx.x ? (P.chunks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int s_len = P.s_len;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane != 0) return;
+    const uint64_t policy = policy_evict_first();
+    int issued = 0;
+    const int produce = (P.flags & kFlagStallProducer) ? 0 : my_chunks;
+    for (int k = 0; k < produce; ++k) {
+      const int st = k % NS;
+      if (k >= NS && !mbar_wait(empty0 + 8u * st, ((k / NS) - 1) & 1, abort_flag, P.err,
+                                P.wait_timeout_ns, kSiteProducerEmpty))
+        break;
+      const int64_t chunk = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
+      const int64_t u0 = chunk * P.units_per_chunk;
+      const int64_t left = P.units - u0;
+      const int nu = left < P.units_per_chunk ? (int)left : P.units_per_chunk;
+      const uint32_t kb = (uint32_t)nu * (uint32_t)s_len * (uint32_t)(D * 2);
+      const uint32_t qb = (uint32_t)nu * (uint32_t)(G * D * 2);
+      const uint32_t bar = full0 + 8u * st;
+      const uint32_t dst = ring0 + (uint32_t)st * P.stage_bytes;
+      mbar_arrive_expect_tx(bar, 2 * kb + qb);
+      bulk_g2s(dst, P.K + u0 * s_len * D, kb, bar, policy);
+      bulk_g2s(dst + P.v_off, P.V + u0 * s_len * D, kb, bar, policy);
+      bulk_g2s(dst + P.q_off, P.Q + u0 * G * D, qb, bar, policy);
+      issued = k + 1;
+    }
+    // Never leave the CTA with copies in flight into its shared memory.
+    const int first = issued > NS ? issued - NS : 0;
+    for (int k = first; k < issued; ++k)
+      mbar_wait(full0 + 8u * (k % NS), (k / NS) & 1, nullptr, P.err, P.wait_timeout_ns,
+                kSiteDrain);
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int cw = warp - 1;
+  float* sc = reinterpret_cast<float*>(smem + P.sc_off) + cw * T::SC;
+  const int r0 = lane / T::LPR;
+  const int cl = lane % T::LPR;
+  const int ul = OutputMap<D, SMAX, G>::unit(lane);
+  const int CT = P.tiles_per_chunk;
+  const int jobs = my_chunks * CT;
+  for (int f = cw; f < jobs; f += ncw) {
+    const int k = f / CT;
+    const int j = f - k * CT;
+    const int st = k % NS;
+    if (!mbar_wait(full0 + 8u * st, (k / NS) & 1, abort_flag, P.err, P.wait_timeout_ns,
+                   kSiteConsumerFull))
+      break;
+    const int64_t chunk = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
+    const int64_t tile_u0 = chunk * P.units_per_chunk + (int64_t)j * T::NU;
+    const int64_t left = P.units - tile_u0;
+    const int uv = left <= 0 ? 0 : (left < T::NU ? (int)left : T::NU);
+    float acc[G][8];
+    if (uv > 0) {
+      const uint32_t sbase = ring0 + (uint32_t)st * P.stage_bytes;
+      const uint32_t kbase = sbase + (uint32_t)(j * T::NU * s_len) * (D * 2) + cl * 16;
+      const uint32_t vbase = kbase + P.v_off;
+      const uint32_t qbase = sbase + P.q_off + (uint32_t)(j * T::NU) * (G * D * 2) + cl * 16;
+      float q[G][8];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (ul < uv) w = lds128(qbase + (uint32_t)(ul * G + g) * (D * 2));
+        unpack8(w, q[g]);
+      }
+      auto row_off = [&](int p) -> uint32_t {
+        const int r = p * T::RPP + r0;
+        return (uint32_t)((r / SMAX) * s_len + (r % SMAX)) * (D * 2);
+      };
+      auto loadK = [&](int p) { return lds128(kbase + row_off(p)); };
+      auto loadV = [&](int p) { return lds128(vbase + row_off(p)); };
+      attend_tile<D, SMAX, G>(q, loadK, loadV, s_len, uv, P.scale_log2, sc, lane, acc);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8u * st);  // stage's shared reads are done
+    if (uv > 0 && ul < uv && OutputMap<D, SMAX, G>::writer(lane)) {
+      uint16_t* orow = P.O + (tile_u0 + ul) * (G * D) + cl * 8;
+#pragma unroll
+      for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
+    }
+  }
+}
+
+#define FMHA_CAT2(a, b) a##b
+#define FMHA_CAT(a, b) FMHA_CAT2(a, b)
+
+// Lookup of the instantiation for (SMAX, G) at this translation unit's D.
+KernelFn FMHA_CAT(bulk_kernel_d, FMHA_HEAD_DIM)(int smax, int g) {
+  constexpr int D = FMHA_HEAD_DIM;
+#define FMHA_G(SM)                                      \
+  switch (g) {                                          \
+    case 1: return decode_bulk_kernel<D, SM, 1>;        \
+    case 2: return decode_bulk_kernel<D, SM, 2>;        \
+    case 4: return decode_bulk_kernel<D, SM, 4>;        \
+    case 8: return decode_bulk_kernel<D, SM, 8>;        \
+    default: return nullptr;                            \
+  }
+  switch (smax) {
+    case 1: FMHA_G(1)
+    case 2: FMHA_G(2)
+    case 4: FMHA_G(4)
+    case 8: FMHA_G(8)
+    case 16: FMHA_G(16)
+    default: return nullptr;
+  }
+#undef FMHA_G
+}
+
+}  // namespace fmha

@@ -1,0 +1,364 @@
+// decode_common.cuh -- shared device code of the sm_100a decode-attention
+// kernels: launch parameters, PTX wrappers (mbarrier, cp.async.bulk, streaming
+// loads/stores), and the per-warp tile computation both kernel families use.
+//
+// Work decomposition. A *unit* is one (batch row, kv head) pair: in the
+// [B,H,S,D] layout its K slab (S x D bf16), its V slab, its G = Hq/Hkv query
+// rows and its G output rows are each contiguous, and consecutive units are
+// adjacent, so any run of units is one contiguous byte range per tensor.
+// Unit u's K starts at u*S*D, its Q and O at u*G*D. (The reference gives each
+// thread block 16 query heads of one batch row and indexes K/V by query head,
+// fmha_vectorized_fma_kernel.hpp:113-135; here a warp owns whole kv heads so
+// K and V are read once however many query heads share them.)
+//
+// A *tile* is the work of one warp: ROWS = max(SMAX, RPP) K/V rows, i.e. NU =
+// ROWS/SMAX units. Each row is D bf16 = D/8 lanes x 16 bytes, so a warp covers
+// RPP = 256/D rows per 16-byte vector access. Lane l owns columns
+// (l % LPR)*8 .. +8 of rows p*RPP + l/LPR, p = 0..NP-1; every row a lane
+// touches belongs to the same unit.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fmha {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+constexpr int kBulkThreads = 288;  // 1 producer warp + 8 consumer warps
+constexpr int kLdgThreads = 256;   // 8 warps
+constexpr int kHdrBytes = 1024;    // mbarriers + abort flag of the bulk kernel
+constexpr int kMaxStages = 48;
+constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kStallTimeoutNs = 20000000ull;   // 20 ms (test hook)
+// Test hook: the bulk producer issues no copies, so every consumer wait runs
+// into its bound and the kernel must report FMHA_ERR_DEVICE_TIMEOUT and exit.
+constexpr int kFlagStallProducer = 1;
+
+// Device error word (first error wins). Low byte: fmha_status_t value;
+// bits 8..15: the wait site that gave up.
+enum : unsigned { kSiteProducerEmpty = 1, kSiteConsumerFull = 2, kSiteDrain = 3 };
+
+struct Params {
+  const uint16_t* Q;
+  const uint16_t* K;
+  const uint16_t* V;
+  uint16_t* O;
+  unsigned int* err;  // device error word (a __device__ variable of the API unit)
+  unsigned long long wait_timeout_ns;  // bound on every mbarrier wait
+  int flags;                           // kFlag* bits
+  int64_t units;     // batch * num_heads_kv
+  int s_len;         // seqlen_kv, 1..SMAX
+  float scale_log2;  // log2(e) / sqrt(D)
+  // bulk family only
+  int units_per_chunk;  // CU = tiles_per_chunk * NU
+  int tiles_per_chunk;  // CT
+  int stages;           // NS
+  int chunks;           // ceil(units / CU)
+  uint32_t stage_bytes; // bytes per ring stage (128-aligned)
+  uint32_t v_off;       // V offset inside a stage (K at 0)
+  uint32_t q_off;       // Q offset inside a stage
+  uint32_t sc_off;      // per-warp score scratch offset in shared memory
+  uint32_t ring_off;    // first stage offset in shared memory
+};
+
+template <int D, int SMAX, int G>
+struct TileShape {
+  static_assert(D == 128 || D == 256, "head_dim");
+  static_assert(SMAX == 1 || SMAX == 2 || SMAX == 4 || SMAX == 8 || SMAX == 16, "SMAX");
+  static constexpr int LPR = D / 8;                     // lanes per row
+  static constexpr int RPP = 32 / LPR;                  // rows per 16B access
+  static constexpr int ROWS = SMAX > RPP ? SMAX : RPP;  // rows per tile
+  static constexpr int NU = ROWS / SMAX;                // units per tile
+  static constexpr int NP = ROWS / RPP;                 // rows per lane
+  static constexpr int LOG_LPR = LPR == 32 ? 5 : 4;
+  static constexpr int LOG_NP = NP == 16 ? 4 : NP == 8 ? 3 : NP == 4 ? 2 : NP == 2 ? 1 : 0;
+  static constexpr int HOLD_SHIFT = LOG_LPR - LOG_NP;   // see reduce_scatter
+  static constexpr int SC = G * ROWS;                   // scores per tile
+  static_assert(NP <= LPR, "reduce-scatter needs NP <= LPR");
+};
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void report_device_error(unsigned* err, unsigned status,
+                                                    unsigned site) {
+  if (err) atomicCAS(err, 0u, status | (site << 8));
+}
+
+// Bounded wait on an mbarrier phase. Returns false if `abort_flag` was raised
+// by another warp or if the wait ran past `timeout_ns` (then the device
+// error word is set and the abort flag raised). Never traps.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort_flag, unsigned* err,
+                                          unsigned long long timeout_ns, unsigned site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (abort_flag && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        report_device_error(err, 5u /* FMHA_ERR_DEVICE_TIMEOUT */, site);
+        if (abort_flag) *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 1-D bulk copy global -> shared (no tensor map, no multicast), completing
+// `bytes` of transaction count on the mbarrier. dst/src 16-byte aligned, bytes
+// a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Streaming 16-byte global load: read-only path, no L1 allocation, 256-byte
+// L2 fetch granularity (every byte of a K/V slab is used exactly once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void stg_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// ------------------------------------------------------------ arithmetic
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ void unpack8(const uint4 w, float (&f)[8]) {
+  f[0] = bf_lo(w.x); f[1] = bf_hi(w.x);
+  f[2] = bf_lo(w.y); f[3] = bf_hi(w.y);
+  f[4] = bf_lo(w.z); f[5] = bf_hi(w.z);
+  f[6] = bf_lo(w.w); f[7] = bf_hi(w.w);
+}
+
+__device__ __forceinline__ float dot8(const float (&q)[8], const uint4 k) {
+  float a = q[0] * bf_lo(k.x);
+  a = fmaf(q[1], bf_hi(k.x), a);
+  a = fmaf(q[2], bf_lo(k.y), a);
+  a = fmaf(q[3], bf_hi(k.y), a);
+  a = fmaf(q[4], bf_lo(k.z), a);
+  a = fmaf(q[5], bf_hi(k.z), a);
+  a = fmaf(q[6], bf_lo(k.w), a);
+  a = fmaf(q[7], bf_hi(k.w), a);
+  return a;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 pack8_f16(const float (&a)[8]) {
+  return make_uint4(pack_half2(a[0], a[1]), pack_half2(a[2], a[3]), pack_half2(a[4], a[5]),
+                    pack_half2(a[6], a[7]));
+}
+
+// Sums N partial values across the LPR lanes of a row group, scattering the
+// results: each halving step trades half of the remaining values with the
+// partner lane (xor `o`), so N values need N-1 shuffles instead of
+// N*log2(LPR). Afterwards lane cl holds the full sum of index
+// cl >> HOLD_SHIFT (replicated over the low HOLD_SHIFT lane bits).
+template <int N, int LPR>
+__device__ __forceinline__ float reduce_scatter(float (&v)[N], int cl) {
+#pragma unroll
+  for (int o = LPR / 2, n = N; o >= 1; o >>= 1) {
+    if (n > 1) {
+      const int half = n / 2;
+      const bool upper = (cl & o) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(kFullMask, send, o);
+      }
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(kFullMask, v[0], o);
+    }
+  }
+  return v[0];
+}
+
+// One warp computes one tile: scores, softmax and P.V for NU units x G query
+// heads. `loadK(p)` / `loadV(p)` return this lane's 16 bytes of row
+// p*RPP + r0 (only called for valid rows). `q[g]` holds this lane's 8 query
+// columns of head g (fp32). `sc` is this warp's G*ROWS float scratch in shared
+// memory. On return acc[g][0..7] is this lane's 8 output columns of head g of
+// its unit (after the cross-row-group sum when two row groups share a unit).
+//
+// Math per (unit, head): x_s = (q . k_s) * log2(e)/sqrt(D) for s < s_len
+// (-inf beyond, the reference's max_seqlen 16 tile masking); p_s =
+// 2^(x_s - max) / sum; o = sum_s p_s v_s. P stays fp32 (the reference's
+// vectorized kernel keeps fp32 P, fmha_vectorized_fma_kernel.hpp:256,281-287;
+// its host oracle rounds P to bf16, fmha_host.cpp:225, which the fp16-output
+// tolerance of this library does not allow).
+template <int D, int SMAX, int G, class LoadK, class LoadV>
+__device__ __forceinline__ void attend_tile(const float (&q)[G][8], LoadK loadK, LoadV loadV,
+                                            int s_len, int units_valid, float scale_log2,
+                                            float* sc, int lane, float (&acc)[G][8]) {
+  using T = TileShape<D, SMAX, G>;
+  const int r0 = lane / T::LPR;
+  const int cl = lane % T::LPR;
+  auto row_ok = [&](int p) {
+    const int r = p * T::RPP + r0;
+    return (r % SMAX) < s_len && (r / SMAX) < units_valid;
+  };
+
+  __syncwarp();  // previous tile's readers of sc are done
+
+  // 1. scores
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float v[T::NP];
+#pragma unroll
+    for (int p = 0; p < T::NP; ++p) v[p] = row_ok(p) ? dot8(q[g], loadK(p)) : 0.0f;
+    const float s = reduce_scatter<T::NP, T::LPR>(v, cl);
+    const int pi = cl >> T::HOLD_SHIFT;
+    if ((cl & ((1 << T::HOLD_SHIFT) - 1)) == 0) {
+      sc[g * T::ROWS + pi * T::RPP + r0] = row_ok(pi) ? s * scale_log2 : -INFINITY;
+    }
+  }
+  __syncwarp();
+
+  // 2. softmax over segments of SMAX consecutive scores (one unit, one head)
+#pragma unroll
+  for (int base = 0; base < T::SC; base += 32) {
+    const int e = base + lane;
+    const float x = e < T::SC ? sc[e] : -INFINITY;
+    float m = x;
+#pragma unroll
+    for (int o = 1; o < SMAX; o <<= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
+    const float ex = (m == -INFINITY) ? 0.0f : exp2f(x - m);
+    float sum = ex;
+#pragma unroll
+    for (int o = 1; o < SMAX; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
+    if (e < T::SC) sc[e] = sum > 0.0f ? ex / sum : 0.0f;
+  }
+  __syncwarp();
+
+  // 3. P.V
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[g][c] = 0.0f;
+#pragma unroll
+  for (int p = 0; p < T::NP; ++p) {
+    if (!row_ok(p)) continue;
+    float vf[8];
+    unpack8(loadV(p), vf);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float pr = sc[g * T::ROWS + p * T::RPP + r0];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[g][c] = fmaf(pr, vf[c], acc[g][c]);
+    }
+  }
+  if constexpr (T::NU == 1 && T::RPP == 2) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[g][c] += __shfl_xor_sync(kFullMask, acc[g][c], 16);
+  }
+}
+
+// Which lanes store the output, and for which unit of the tile.
+template <int D, int SMAX, int G>
+struct OutputMap {
+  using T = TileShape<D, SMAX, G>;
+  __device__ __forceinline__ static int unit(int lane) { return (lane / T::LPR) / SMAX; }
+  __device__ __forceinline__ static bool writer(int lane) {
+    return !(T::NU == 1 && T::RPP == 2) || (lane / T::LPR) == 0;
+  }
+};
+
+// Tiles per warp step of the ldg family: enough for 16 K rows and 16 V rows
+// per lane in flight, fewer when many query heads share a kv head (their Q
+// rows are loaded too).
+template <int D, int SMAX, int G>
+struct LdgTpi {
+  using T = TileShape<D, SMAX, G>;
+  static constexpr int by_rows = 16 / T::NP;
+  static constexpr int by_q = G >= 8 ? 1 : 8 / G;
+  static constexpr int value = by_rows < by_q ? by_rows : by_q;
+};
+
+// Kernel entry points (defined in decode_bulk.cu / decode_ldg.cu).
+template <int D, int SMAX, int G>
+__global__ void decode_bulk_kernel(const Params P);
+template <int D, int SMAX, int G, int TPI>
+__global__ void decode_ldg_kernel(const Params P);
+
+using KernelFn = void (*)(const Params);
+
+// Per-head_dim lookups of the instantiation for (SMAX, G); nullptr if absent.
+KernelFn bulk_kernel_d128(int smax, int g);
+KernelFn bulk_kernel_d256(int smax, int g);
+KernelFn ldg_kernel_d128(int smax, int g);
+KernelFn ldg_kernel_d256(int smax, int g);
+
+}  // namespace fmha

@@ -1,0 +1,104 @@
+// decode_ldg.cu -- "ldg" kernel family: persistent warps that load their
+// tiles' K/V rows straight into registers with 16-byte streaming loads
+// (ld.global.nc, no L1 allocation, 256-byte L2 fetch), then compute.
+//
+// Each warp takes TPI consecutive tiles per step (tiles t0 .. t0+TPI-1, t0
+// advancing by TPI * total warps) and issues every load of the step before
+// the first arithmetic, so each warp keeps TPI*NP*2 16-byte loads per lane in
+// flight. This is the register-resident counterpart of the bulk family and is
+// kept as the comparison point the dispatcher measures against.
+//
+// Compiled once per head_dim: -DFMHA_HEAD_DIM=128 or 256.
+#include "decode_common.cuh"
+
+#ifndef FMHA_HEAD_DIM
+#error "compile with -DFMHA_HEAD_DIM=128 or 256"
+#endif
+
+namespace fmha {
+
+template <int D, int SMAX, int G, int TPI>
+__global__ void __launch_bounds__(kLdgThreads) decode_ldg_kernel(const Params P) {
+  using T = TileShape<D, SMAX, G>;
+  constexpr int WPB = kLdgThreads / 32;
+  __shared__ float sc_all[WPB][T::SC];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  float* sc = sc_all[warp];
+  const int r0 = lane / T::LPR;
+  const int cl = lane % T::LPR;
+  const int ul = OutputMap<D, SMAX, G>::unit(lane);
+  const int s_len = P.s_len;
+  const int64_t tiles = (P.units + T::NU - 1) / T::NU;
+  const int64_t gw = (int64_t)blockIdx.x * WPB + warp;
+  const int64_t stride = (int64_t)gridDim.x * WPB * TPI;
+
+  for (int64_t t0 = gw * TPI; t0 < tiles; t0 += stride) {
+    uint4 kr[TPI][T::NP], vr[TPI][T::NP], qr[TPI][G];
+    int uv[TPI];
+#pragma unroll
+    for (int i = 0; i < TPI; ++i) {
+      const int64_t tile_u0 = (t0 + i) * T::NU;
+      const int64_t left = P.units - tile_u0;
+      uv[i] = left <= 0 ? 0 : (left < T::NU ? (int)left : T::NU);
+      const uint16_t* kb = P.K + tile_u0 * s_len * D + cl * 8;
+      const uint16_t* vb = P.V + tile_u0 * s_len * D + cl * 8;
+#pragma unroll
+      for (int p = 0; p < T::NP; ++p) {
+        const int r = p * T::RPP + r0;
+        const int64_t off = (int64_t)((r / SMAX) * s_len + (r % SMAX)) * D;
+        const bool ok = (r % SMAX) < s_len && (r / SMAX) < uv[i];
+        kr[i][p] = ok ? ldg_stream(kb + off) : make_uint4(0, 0, 0, 0);
+        vr[i][p] = ok ? ldg_stream(vb + off) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        qr[i][g] = ul < uv[i] ? ldg_stream(P.Q + (tile_u0 + ul) * (G * D) + g * D + cl * 8)
+                              : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < TPI; ++i) {
+      if (uv[i] <= 0) continue;  // warp-uniform
+      float q[G][8];
+#pragma unroll
+      for (int g = 0; g < G; ++g) unpack8(qr[i][g], q[g]);
+      float acc[G][8];
+      auto loadK = [&](int p) { return kr[i][p]; };
+      auto loadV = [&](int p) { return vr[i][p]; };
+      attend_tile<D, SMAX, G>(q, loadK, loadV, s_len, uv[i], P.scale_log2, sc, lane, acc);
+      if (ul < uv[i] && OutputMap<D, SMAX, G>::writer(lane)) {
+        uint16_t* orow = P.O + ((t0 + i) * T::NU + ul) * (G * D) + cl * 8;
+#pragma unroll
+        for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
+      }
+    }
+  }
+}
+
+#define FMHA_CAT2(a, b) a##b
+#define FMHA_CAT(a, b) FMHA_CAT2(a, b)
+
+KernelFn FMHA_CAT(ldg_kernel_d, FMHA_HEAD_DIM)(int smax, int g) {
+  constexpr int D = FMHA_HEAD_DIM;
+#define FMHA_K(SM, GG) decode_ldg_kernel<D, SM, GG, LdgTpi<D, SM, GG>::value>
+#define FMHA_G(SM)                    \
+  switch (g) {                        \
+    case 1: return FMHA_K(SM, 1);     \
+    case 2: return FMHA_K(SM, 2);     \
+    case 4: return FMHA_K(SM, 4);     \
+    case 8: return FMHA_K(SM, 8);     \
+    default: return nullptr;          \
+  }
+  switch (smax) {
+    case 1: FMHA_G(1)
+    case 2: FMHA_G(2)
+    case 4: FMHA_G(4)
+    case 8: FMHA_G(8)
+    case 16: FMHA_G(16)
+    default: return nullptr;
+  }
+#undef FMHA_G
+#undef FMHA_K
+}
+
+}  // namespace fmha

@@ -1,0 +1,370 @@
+// fmha_api.cu -- the extern "C" boundary of libfmha_b200.so (include/fmha.h):
+// argument validation, per-device launch planning and dispatch to the
+// head_dim/seqlen/group-specialised kernels, the device error word, and the
+// seeded input generator used by the benchmark/validation harness.
+//
+// Reference interface replaced: launch_fmha_mfma_4x4x4
+// (fmha_mfma_4x4x4_kernel.hpp:370-389), which launched with a caller-chosen
+// grid, did no validation and silently treated any head_dim != 128 as 256.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "../../include/fmha.h"
+#include "decode_common.cuh"
+
+namespace fmha {
+
+__device__ unsigned int g_fmha_device_error;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+  int smem_optin = 0;
+  unsigned int* err = nullptr;  // device address of g_fmha_device_error
+};
+
+std::mutex g_mu;
+std::atomic<int> g_test_stall{0};
+DeviceInfo g_dev[kMaxDevices];
+std::set<std::pair<const void*, int>> g_smem_set;      // (kernel, device) with smem attr set
+struct OccEntry {
+  const void* fn;
+  int dev;
+  int blocks;
+};
+OccEntry g_occ[512];
+int g_occ_n = 0;
+
+fmha_status_t device_info(DeviceInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return FMHA_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return FMHA_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+        cudaSuccess)
+      return FMHA_ERR_CUDA;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fmha_device_error) != cudaSuccess) return FMHA_ERR_CUDA;
+    d.err = static_cast<unsigned int*>(p);
+    d.ready = true;
+  }
+  *out = d;
+  return FMHA_OK;
+}
+
+// Sets the kernel's dynamic shared-memory limit once per (kernel, device).
+fmha_status_t ensure_smem(KernelFn fn, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(fn), dev);
+  if (g_smem_set.count(key)) return FMHA_OK;
+  // The limit is set to the device maximum, so one call covers every plan.
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return FMHA_ERR_CUDA;
+  g_smem_set.insert(key);
+  return FMHA_OK;
+}
+
+fmha_status_t blocks_per_sm(KernelFn fn, int threads, int* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < g_occ_n; ++i)
+    if (g_occ[i].fn == reinterpret_cast<const void*>(fn) && g_occ[i].dev == dev) {
+      *out = g_occ[i].blocks;
+      return FMHA_OK;
+    }
+  int b = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, threads, 0) != cudaSuccess)
+    return FMHA_ERR_CUDA;
+  if (b < 1) b = 1;
+  if (g_occ_n < 512) g_occ[g_occ_n++] = {reinterpret_cast<const void*>(fn), dev, b};
+  *out = b;
+  return FMHA_OK;
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v && *v) ? std::atoi(v) : dflt;
+}
+
+int smax_for(int s) {
+  int m = 1;
+  while (m < s) m <<= 1;
+  return m;
+}
+
+int rows_per_access(int d) { return 256 / d; }
+
+// Per-shape default family. Filled from B200 measurements (bench.py
+// --sweep); the bulk family is the default until a shape measures better
+// with ldg.
+int auto_variant(int /*d*/, int /*s*/, int /*g*/) {
+  static const int forced = env_int("FMHA_VARIANT", 0);
+  if (forced == FMHA_VARIANT_BULK || forced == FMHA_VARIANT_LDG) return forced;
+  return FMHA_VARIANT_BULK;
+}
+
+fmha_status_t check_args(const void* Q, const void* K, const void* V, void* O, int batch,
+                         int hq, int hkv, int s, int d) {
+  if (batch < 0 || hq <= 0 || hkv <= 0 || s <= 0 || d <= 0) return FMHA_ERR_INVALID_ARG;
+  if (hq % hkv != 0) return FMHA_ERR_INVALID_ARG;
+  if (batch > 0 && (!Q || !K || !V || !O)) return FMHA_ERR_INVALID_ARG;
+  if (d != 128 && d != 256) return FMHA_ERR_UNSUPPORTED;
+  if (s > 16) return FMHA_ERR_UNSUPPORTED;
+  const int g = hq / hkv;
+  if (g != 1 && g != 2 && g != 4 && g != 8) return FMHA_ERR_UNSUPPORTED;
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) |
+                        reinterpret_cast<uintptr_t>(V) | reinterpret_cast<uintptr_t>(O);
+  if (mis & 15u) return FMHA_ERR_MISALIGNED;
+  // Offsets are 64-bit throughout; keep the unit count within int32 chunking.
+  if ((int64_t)batch * hkv > (int64_t)1 << 30) return FMHA_ERR_UNSUPPORTED;
+  return FMHA_OK;
+}
+
+fmha_status_t launch_bulk(Params P, int d, int smax, int g, const DeviceInfo& dev,
+                          cudaStream_t stream) {
+  KernelFn fn = d == 128 ? bulk_kernel_d128(smax, g) : bulk_kernel_d256(smax, g);
+  if (!fn) return FMHA_ERR_UNSUPPORTED;
+  const int rpp = rows_per_access(d);
+  const int rows = smax > rpp ? smax : rpp;
+  const int nu = rows / smax;
+  const int s = P.s_len;
+  const int64_t tile_bytes = (int64_t)nu * (2LL * s * d * 2 + (int64_t)g * d * 2);
+  const int target = env_int("FMHA_STAGE_BYTES", 32768);
+  int ct = (int)(target / tile_bytes);
+  if (ct < 1) ct = 1;
+  const int cu = ct * nu;
+  const uint32_t kb = (uint32_t)cu * s * d * 2;
+  const uint32_t qb = (uint32_t)cu * g * d * 2;
+  const uint32_t stage = (2 * kb + qb + 127u) & ~127u;
+  const uint32_t sc_off = kHdrBytes;
+  const uint32_t sc_bytes = (uint32_t)(kBulkThreads / 32 - 1) * g * rows * 4;
+  const uint32_t ring_off = (sc_off + sc_bytes + 1023u) & ~1023u;
+  // One CTA per SM by default (the whole shared memory); FMHA_BULK_CTAS_PER_SM
+  // splits the SM's 228 KiB (1 KiB reserved per CTA) between several rings.
+  const int ctas_per_sm = env_int("FMHA_BULK_CTAS_PER_SM", 1) > 1 ? env_int("FMHA_BULK_CTAS_PER_SM", 1) : 1;
+  int budget = dev.smem_optin;
+  if (ctas_per_sm > 1 && 233472 / ctas_per_sm - 1024 < budget) budget = 233472 / ctas_per_sm - 1024;
+  int ns = (int)((budget - (int64_t)ring_off) / stage);
+  const int ns_cap = env_int("FMHA_STAGES", kMaxStages);
+  if (ns > ns_cap) ns = ns_cap;
+  if (ns > kMaxStages) ns = kMaxStages;
+  if (ns < 2) return FMHA_ERR_UNSUPPORTED;
+  const uint32_t smem = ring_off + (uint32_t)ns * stage;
+  P.units_per_chunk = cu;
+  P.tiles_per_chunk = ct;
+  P.stages = ns;
+  P.chunks = (int)((P.units + cu - 1) / cu);
+  P.stage_bytes = stage;
+  P.v_off = kb;
+  P.q_off = 2 * kb;
+  P.sc_off = sc_off;
+  P.ring_off = ring_off;
+  fmha_status_t st = ensure_smem(fn, dev.smem_optin);
+  if (st != FMHA_OK) return st;
+  int grid = dev.sms * ctas_per_sm;
+  if (grid > P.chunks) grid = P.chunks;
+  fn<<<grid, kBulkThreads, smem, stream>>>(P);
+  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+}
+
+template <int D>
+int ldg_tpi(int smax, int g) {
+#define FMHA_T(SM)                                  \
+  switch (g) {                                      \
+    case 1: return LdgTpi<D, SM, 1>::value;         \
+    case 2: return LdgTpi<D, SM, 2>::value;         \
+    case 4: return LdgTpi<D, SM, 4>::value;         \
+    default: return LdgTpi<D, SM, 8>::value;        \
+  }
+  switch (smax) {
+    case 1: FMHA_T(1)
+    case 2: FMHA_T(2)
+    case 4: FMHA_T(4)
+    case 8: FMHA_T(8)
+    default: FMHA_T(16)
+  }
+#undef FMHA_T
+}
+
+fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev,
+                         cudaStream_t stream) {
+  KernelFn fn = d == 128 ? ldg_kernel_d128(smax, g) : ldg_kernel_d256(smax, g);
+  if (!fn) return FMHA_ERR_UNSUPPORTED;
+  const int rpp = rows_per_access(d);
+  const int rows = smax > rpp ? smax : rpp;
+  const int nu = rows / smax;
+  const int tpi = d == 128 ? ldg_tpi<128>(smax, g) : ldg_tpi<256>(smax, g);
+  const int64_t tiles = (P.units + nu - 1) / nu;
+  const int wpb = kLdgThreads / 32;
+  int bps = 1;
+  fmha_status_t st = blocks_per_sm(fn, kLdgThreads, &bps);
+  if (st != FMHA_OK) return st;
+  const int64_t need = (tiles + (int64_t)wpb * tpi - 1) / ((int64_t)wpb * tpi);
+  int64_t grid = (int64_t)dev.sms * bps;
+  if (grid > need) grid = need;
+  fn<<<(unsigned)grid, kLdgThreads, 0, stream>>>(P);
+  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+}
+
+// splitmix64 finaliser (Steele, Lea, Flood, OOPSLA 2014).
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ uint16_t gen_one(uint64_t key, uint64_t e) {
+  int64_t t = 0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const uint64_t h = mix64(key + e * 3u + (uint64_t)j);
+    t += (int64_t)(h & 0xffffu) + (int64_t)((h >> 16) & 0xffffu) +
+         (int64_t)((h >> 32) & 0xffffu) + (int64_t)(h >> 48);
+  }
+  const int64_t num = 2 * t + 12 - 12 * 65536;
+  const float x = (float)num * (1.0f / 131072.0f);  // exact: |num| < 2^24
+  uint32_t u = __float_as_uint(x);
+  u += 0x7fffu + ((u >> 16) & 1u);  // bf16 round to nearest even (x is finite)
+  return (uint16_t)(u >> 16);
+}
+
+__global__ void fill_normal_bf16_kernel(uint16_t* __restrict__ dst, int64_t n, uint64_t key,
+                                        int64_t offset) {
+  const int64_t groups = (n + 7) / 8;
+  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < groups;
+       gi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i0 = gi * 8;
+    if (i0 + 8 <= n) {
+      uint32_t w[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t lo = gen_one(key, (uint64_t)(offset + i0 + 2 * c));
+        const uint32_t hi = gen_one(key, (uint64_t)(offset + i0 + 2 * c + 1));
+        w[c] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4*>(dst + i0) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int64_t i = i0; i < n; ++i) dst[i] = gen_one(key, (uint64_t)(offset + i));
+    }
+  }
+}
+
+}  // namespace
+}  // namespace fmha
+
+using namespace fmha;
+
+extern "C" {
+
+fmha_status_t fmha_forward_variant(const void* Q, const void* K, const void* V, void* O,
+                                   int batch, int num_heads_q, int num_heads_kv, int seqlen_kv,
+                                   int head_dim, int variant, fmha_stream_t stream) {
+  fmha_status_t st =
+      check_args(Q, K, V, O, batch, num_heads_q, num_heads_kv, seqlen_kv, head_dim);
+  if (st != FMHA_OK) return st;
+  if (variant < FMHA_VARIANT_AUTO || variant > FMHA_VARIANT_LDG) return FMHA_ERR_INVALID_ARG;
+  if (batch == 0) return FMHA_OK;
+  DeviceInfo dev;
+  st = device_info(&dev);
+  if (st != FMHA_OK) return st;
+  const int g = num_heads_q / num_heads_kv;
+  const int smax = smax_for(seqlen_kv);
+  Params P;
+  std::memset(&P, 0, sizeof(P));
+  P.Q = static_cast<const uint16_t*>(Q);
+  P.K = static_cast<const uint16_t*>(K);
+  P.V = static_cast<const uint16_t*>(V);
+  P.O = static_cast<uint16_t*>(O);
+  P.err = dev.err;
+  P.wait_timeout_ns = kWaitTimeoutNs;
+  if (g_test_stall.load()) {
+    P.flags |= kFlagStallProducer;
+    P.wait_timeout_ns = kStallTimeoutNs;
+    variant = FMHA_VARIANT_BULK;
+  }
+  P.units = (int64_t)batch * num_heads_kv;
+  P.s_len = seqlen_kv;
+  P.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+  if (variant == FMHA_VARIANT_AUTO) variant = auto_variant(head_dim, seqlen_kv, g);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return variant == FMHA_VARIANT_LDG ? launch_ldg(P, head_dim, smax, g, dev, s)
+                                     : launch_bulk(P, head_dim, smax, g, dev, s);
+}
+
+fmha_status_t fmha_forward(const void* Q, const void* K, const void* V, void* O, int batch,
+                           int num_heads_q, int num_heads_kv, int seqlen_kv, int head_dim,
+                           fmha_stream_t stream) {
+  return fmha_forward_variant(Q, K, V, O, batch, num_heads_q, num_heads_kv, seqlen_kv, head_dim,
+                              FMHA_VARIANT_AUTO, stream);
+}
+
+const char* fmha_status_string(fmha_status_t status) {
+  switch (status) {
+    case FMHA_OK: return "FMHA_OK";
+    case FMHA_ERR_INVALID_ARG: return "FMHA_ERR_INVALID_ARG: invalid argument";
+    case FMHA_ERR_UNSUPPORTED: return "FMHA_ERR_UNSUPPORTED: unsupported shape";
+    case FMHA_ERR_MISALIGNED: return "FMHA_ERR_MISALIGNED: pointer not 16-byte aligned";
+    case FMHA_ERR_CUDA: return "FMHA_ERR_CUDA: CUDA runtime error";
+    case FMHA_ERR_DEVICE_TIMEOUT: return "FMHA_ERR_DEVICE_TIMEOUT: a kernel wait timed out";
+    default: return "FMHA_ERR_UNKNOWN";
+  }
+}
+
+fmha_status_t fmha_device_error(int* code) {
+  if (!code) return FMHA_ERR_INVALID_ARG;
+  DeviceInfo dev;
+  fmha_status_t st = device_info(&dev);
+  if (st != FMHA_OK) return st;
+  if (cudaDeviceSynchronize() != cudaSuccess) return FMHA_ERR_CUDA;
+  unsigned int v = 0;
+  if (cudaMemcpy(&v, dev.err, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return FMHA_ERR_CUDA;
+  if (v != 0 && cudaMemset(dev.err, 0, sizeof(v)) != cudaSuccess) return FMHA_ERR_CUDA;
+  *code = (int)v;
+  return FMHA_OK;
+}
+
+fmha_status_t fmha_fill_normal_bf16(void* dst, int64_t n, uint64_t seed, uint32_t tensor_id,
+                                    int64_t offset, fmha_stream_t stream) {
+  if (n < 0 || offset < 0) return FMHA_ERR_INVALID_ARG;
+  if (n == 0) return FMHA_OK;
+  if (!dst) return FMHA_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(dst) & 15u) return FMHA_ERR_MISALIGNED;
+  DeviceInfo dev;
+  fmha_status_t st = device_info(&dev);
+  if (st != FMHA_OK) return st;
+  const uint64_t key = mix64(seed ^ mix64(((uint64_t)tensor_id << 32) | 0x5bd1e995u));
+  const int64_t groups = (n + 7) / 8;
+  int64_t grid = (groups + 255) / 256;
+  const int64_t cap = (int64_t)dev.sms * 16;
+  if (grid > cap) grid = cap;
+  fill_normal_bf16_kernel<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint16_t*>(dst), n, key, offset);
+  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+}
+
+void fmha_test_inject_stall(int on) { g_test_stall.store(on ? 1 : 0); }
+
+const char* fmha_version(void) { return "fmha_b200 0.1.0 sm_100a"; }
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+"""CPU tests of the C boundary: the library loads, exports every entry point
+include/fmha.h declares, and rejects bad arguments before touching CUDA (so
+these calls need no GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import fmha_b200
+from fmha_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(fmha_\w+)\s*\(", src))
+    return sorted(names)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = fmha_b200.load()
+    names = declared_symbols()
+    assert "fmha_forward" in names
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version():
+    assert "sm_100a" in fmha_b200.version()
+
+
+BASE = dict(q=16, k=32, v=48, o=64, batch=4, num_heads_q=16, num_heads_kv=16, seqlen_kv=16,
+            head_dim=128)
+
+
+def call(**kw):
+    a = dict(BASE)
+    a.update(kw)
+    return fmha_b200.fmha_forward_ptr(a["q"], a["k"], a["v"], a["o"], a["batch"], a["num_heads_q"],
+                                      a["num_heads_kv"], a["seqlen_kv"], a["head_dim"],
+                                      variant=a.get("variant", "auto"))
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(q=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(o=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(batch=-1), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(num_heads_q=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(num_heads_kv=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(num_heads_q=24, num_heads_kv=16), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(seqlen_kv=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(seqlen_kv=17), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(head_dim=64), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(head_dim=192), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(num_heads_q=48, num_heads_kv=16), _lib.FMHA_ERR_UNSUPPORTED),   # 3 q heads per kv head
+    (dict(num_heads_q=32, num_heads_kv=2), _lib.FMHA_ERR_UNSUPPORTED),    # 16 per kv head
+    (dict(q=24), _lib.FMHA_ERR_MISALIGNED),
+    (dict(v=8), _lib.FMHA_ERR_MISALIGNED),
+    (dict(variant=7), _lib.FMHA_ERR_INVALID_ARG),
+])
+def test_rejected_before_any_cuda_call(kw, status):
+    assert call(**kw) == status
+
+
+def test_empty_batch_is_a_noop():
+    assert call(batch=0, q=0, k=0, v=0, o=0) == _lib.FMHA_OK
+
+
+def test_status_strings():
+    for s in range(6):
+        assert fmha_b200.status_string(s).startswith("FMHA_")
+    assert "UNKNOWN" in fmha_b200.status_string(99)
+
+
+def test_fill_rejects_bad_args():
+    lib = fmha_b200.load()
+    assert lib.fmha_fill_normal_bf16(None, 8, 0, 1, 0, None) == _lib.FMHA_ERR_INVALID_ARG
+    assert lib.fmha_fill_normal_bf16(18, 8, 0, 1, 0, None) == _lib.FMHA_ERR_MISALIGNED
+    assert lib.fmha_fill_normal_bf16(16, -1, 0, 1, 0, None) == _lib.FMHA_ERR_INVALID_ARG
+    assert lib.fmha_fill_normal_bf16(16, 0, 0, 1, 0, None) == _lib.FMHA_OK
+
+
+def test_device_error_needs_pointer():
+    lib = fmha_b200.load()
+    assert lib.fmha_device_error(ctypes.cast(0, ctypes.POINTER(ctypes.c_int))) == \
+        _lib.FMHA_ERR_INVALID_ARG

@@ -1,0 +1,153 @@
+"""CPU tests of the oracle (the checker): pinned against the reference's own
+do_validation (fmha_host.cpp:158-284, compiled from source into oracle/_ref)
+and against the golden fixtures that build produced (tests/golden/)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _packed(x, b, h, s, d):
+    return np.ascontiguousarray(x.reshape(b, h, s, d).transpose(0, 2, 1, 3)).reshape(-1)
+
+
+@pytest.mark.parametrize("b,h,d,seed", [(10, 16, 128, 1), (33, 32, 256, 2), (17, 16, 256, 3),
+                                        (1, 1, 128, 4)])
+def test_thd_ref_faithful_bitexact_vs_reference_build(oracle, b, h, d, seed):
+    if not oracle.ref_available():
+        pytest.skip("reference sources were not available to build oracle/_ref")
+    sl = oracle.ref_generate_seqlens(b, 16)
+    cu = np.concatenate([[0], np.cumsum(sl)]).astype(np.int32)
+    t = int(cu[-1])
+    q = oracle.gen_bf16(b * h * d, seed, 1)
+    k = oracle.gen_bf16(t * h * d, seed, 2)
+    v = oracle.gen_bf16(t * h * d, seed, 3)
+    _, ref_o = oracle.ref_do_validation(q, k, v, sl, b, h, h, d, threads=3)
+    _, mine = oracle.decode_thd(q, k, v, cu, b, h, h, d, p_bf16=True)
+    assert np.array_equal(ref_o, mine)
+
+
+@pytest.mark.parametrize("s", [1, 2, 5, 16])
+def test_bhsd_ref_faithful_bitexact_vs_reference_build(oracle, s):
+    if not oracle.ref_available():
+        pytest.skip("reference build absent")
+    b, h, d = 6, 16, 256
+    q, k, v = oracle.make_inputs_bhsd(b, h, h, s, d, seed=9)
+    sl = np.full(b, s, dtype=np.int32)
+    _, ref_o = oracle.ref_do_validation(q, _packed(k, b, h, s, d), _packed(v, b, h, s, d),
+                                        sl, b, h, h, d)
+    _, mine = oracle.decode_bhsd(q, k, v, b, h, h, s, d, p_bf16=True)
+    assert np.array_equal(ref_o, mine)
+
+
+def test_reference_validation_accepts_its_own_output(oracle):
+    if not oracle.ref_available():
+        pytest.skip("reference build absent")
+    b, h, d = 4, 16, 128
+    sl = oracle.ref_generate_seqlens(b, 16)
+    t = int(sl.sum())
+    q = oracle.gen_bf16(b * h * d, 5, 1)
+    k = oracle.gen_bf16(t * h * d, 5, 2)
+    v = oracle.gen_bf16(t * h * d, 5, 3)
+    ok0, ref_o = oracle.ref_do_validation(q, k, v, sl, b, h, h, d)
+    assert not ok0  # compared against zeros
+    ok1, _ = oracle.ref_do_validation(q, k, v, sl, b, h, h, d, h_o=ref_o)
+    assert ok1
+
+
+def _fixtures():
+    return sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+
+
+def _inputs_for(oracle, f):
+    b, d, seed = int(f["batch"]), int(f["head_dim"]), int(f["seed"])
+    h = int(f["heads"])
+    if str(f["kind"]) == "thd":
+        sl = f["seqlens"]
+        t = int(sl.sum())
+        q = oracle.gen_bf16(b * h * d, seed, 1)
+        k = oracle.gen_bf16(t * h * d, seed, 2)
+        v = oracle.gen_bf16(t * h * d, seed, 3)
+        return q, k, v
+    return oracle.make_inputs_bhsd(b, h, h, int(f["seqlen"]), d, seed)
+
+
+def test_fixtures_present():
+    assert len(_fixtures()) >= 8
+
+
+@pytest.mark.parametrize("path", _fixtures(), ids=os.path.basename)
+def test_oracle_matches_golden(oracle, path):
+    from tests.golden.make_golden import checksum
+    f = np.load(path)
+    q, k, v = _inputs_for(oracle, f)
+    assert int(checksum(q, k, v)) == int(f["input_checksum"]), "generator drifted"
+    b, h, d = int(f["batch"]), int(f["heads"]), int(f["head_dim"])
+    if str(f["kind"]) == "thd":
+        cu = np.concatenate([[0], np.cumsum(f["seqlens"])]).astype(np.int32)
+        _, mine = oracle.decode_thd(q, k, v, cu, b, h, h, d, p_bf16=True)
+    else:
+        _, mine = oracle.decode_bhsd(q, k, v, b, h, h, int(f["seqlen"]), d, p_bf16=True)
+    assert np.array_equal(mine, f["ref_o"])
+
+
+def test_bhsd_equals_thd_after_packing(oracle):
+    b, h, s, d = 5, 16, 7, 128
+    q, k, v = oracle.make_inputs_bhsd(b, h, h, s, d, seed=3)
+    cu = (np.arange(b + 1) * s).astype(np.int32)
+    o1, _ = oracle.decode_bhsd(q, k, v, b, h, h, s, d)
+    o2, _ = oracle.decode_thd(q, _packed(k, b, h, s, d), _packed(v, b, h, s, d), cu, b, h, h, d)
+    assert np.array_equal(o1, o2)
+
+
+def _numpy_attention(q, k, v, b, hq, hkv, s, d):
+    f = lambda x: x.astype(np.uint32) << 16  # noqa: E731
+    Q = f(q).view(np.float32).astype(np.float64).reshape(b, hq, d)
+    K = f(k).view(np.float32).astype(np.float64).reshape(b, hkv, s, d)
+    V = f(v).view(np.float32).astype(np.float64).reshape(b, hkv, s, d)
+    g = hq // hkv
+    K = np.repeat(K, g, axis=1)
+    V = np.repeat(V, g, axis=1)
+    sc = np.einsum("bhd,bhsd->bhs", Q, K) / np.sqrt(d)
+    sc -= sc.max(-1, keepdims=True)
+    p = np.exp(sc)
+    p /= p.sum(-1, keepdims=True)
+    return np.einsum("bhs,bhsd->bhd", p, V).reshape(-1)
+
+
+@pytest.mark.parametrize("hq,hkv,s,d", [(16, 16, 16, 128), (32, 16, 9, 256), (32, 8, 4, 128),
+                                        (16, 2, 16, 256), (8, 8, 1, 256)])
+def test_exact_mode_vs_float64(oracle, hq, hkv, s, d):
+    """GQA is unpinned by the reference (its kernels and oracle index K/V by
+    the query head); the oracle's grouping kvh = h/(Hq/Hkv) is checked against
+    an independent float64 implementation instead."""
+    b = 6
+    q, k, v = oracle.make_inputs_bhsd(b, hq, hkv, s, d, seed=17)
+    o32, _ = oracle.decode_bhsd(q, k, v, b, hq, hkv, s, d)
+    ref = _numpy_attention(q, k, v, b, hq, hkv, s, d)
+    assert np.max(np.abs(o32 - ref)) < 2e-5
+
+
+def test_faithful_differs_from_exact_only_by_p_rounding(oracle):
+    b, h, s, d = 64, 16, 16, 256
+    q, k, v = oracle.make_inputs_bhsd(b, h, h, s, d, seed=4)
+    o_exact, _ = oracle.decode_bhsd(q, k, v, b, h, h, s, d)
+    o_f, _ = oracle.decode_bhsd(q, k, v, b, h, h, s, d, p_bf16=True)
+    diff = np.abs(o_exact - o_f)
+    assert 0 < diff.max() < 2e-2  # bf16 P: ~3 significant digits
+    o1, _ = oracle.decode_bhsd(q, k, v, b, h, h, 1, d)  # S=1: P == 1 exactly
+    o2, _ = oracle.decode_bhsd(q, k, v, b, h, h, 1, d, p_bf16=True)
+    assert np.array_equal(o1, o2)
+
+
+def test_generator_offsets_and_moments(oracle):
+    full = oracle.gen_bf16(100000, 123, 2)
+    part = oracle.gen_bf16(1000, 123, 2, offset=50000)
+    assert np.array_equal(full[50000:51000], part)
+    x = oracle.bf16_to_f32(full).astype(np.float64)
+    assert abs(x.mean()) < 0.02 and abs(x.std() - 1.0) < 0.02
+    assert not np.array_equal(full, oracle.gen_bf16(100000, 124, 2))
+    assert not np.array_equal(full, oracle.gen_bf16(100000, 123, 3))
