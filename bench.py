@@ -269,6 +269,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true",
+                    help="skip the nvidia-smi sampler (profiling runs)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's batch (small profiling cases only)")
     ap.add_argument("--sweep", action="store_true",
                     help="device-time lines for every config and variant (no e2e/cpu)")
     args = ap.parse_args()
@@ -316,8 +320,10 @@ def main():
         return 0
 
     cfg = CONFIGS[args.config]
+    if args.batch > 0:
+        cfg = (args.batch,) + tuple(cfg[1:])
     r = time_config(torch, fmha_b200, cfg, world, rank, args, args.variant, barrier,
-                    max_over_ranks, dev, clocks=True)
+                    max_over_ranks, dev, clocks=not args.no_clocks)
     e2e = None
     if not args.no_e2e:
         e2e = e2e_leg(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev)

@@ -21,8 +21,8 @@
 namespace fmha {
 
 template <int D, int SMAX, int G>
-__global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Params P) {
-  using T = TileShape<D, SMAX, G>;
+__global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const Params P) {
+  using T = Tile16<D, SMAX, G>;
   extern __shared__ __align__(1024) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Para
   const uint32_t full0 = smem_u32(smem);
   const uint32_t empty0 = full0 + 8u * NS;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 16 * NS);
+  volatile int* issued_ctr = abort_flag + 1;  // chunks whose copies are armed
   const uint32_t ring0 = smem_u32(smem + P.ring_off);
 
   if (threadIdx.x == 0) {
@@ -39,6 +40,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Para
       mbar_init(empty0 + 8u * i, P.tiles_per_chunk);
     }
     *abort_flag = 0;
+    *issued_ctr = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -71,6 +73,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Para
       bulk_g2s(dst + P.v_off, P.V + u0 * s_len * D, kb, bar, policy);
       bulk_g2s(dst + P.q_off, P.Q + u0 * G * D, qb, bar, policy);
       issued = k + 1;
+      __threadfence_block();  // the expect_tx above is visible before the count
+      *issued_ctr = issued;
     }
     // Never leave the CTA with copies in flight into its shared memory.
     const int first = issued > NS ? issued - NS : 0;
@@ -85,13 +89,16 @@ __global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Para
   float* sc = reinterpret_cast<float*>(smem + P.sc_off) + cw * T::SC;
   const int r0 = lane / T::LPR;
   const int cl = lane % T::LPR;
-  const int ul = OutputMap<D, SMAX, G>::unit(lane);
   const int CT = P.tiles_per_chunk;
   const int jobs = my_chunks * CT;
   for (int f = cw; f < jobs; f += ncw) {
     const int k = f / CT;
     const int j = f - k * CT;
     const int st = k % NS;
+    // A parity wait is only meaningful once chunk k's phase is armed: before
+    // that the stage may still be in an older phase whose parity differs, and
+    // try_wait.parity would report it complete.
+    if (!wait_issued(issued_ctr, k, abort_flag, P.err, P.wait_timeout_ns)) break;
     if (!mbar_wait(full0 + 8u * st, (k / NS) & 1, abort_flag, P.err, P.wait_timeout_ns,
                    kSiteConsumerFull))
       break;
@@ -99,34 +106,28 @@ __global__ void __launch_bounds__(kBulkThreads, 1) decode_bulk_kernel(const Para
     const int64_t tile_u0 = chunk * P.units_per_chunk + (int64_t)j * T::NU;
     const int64_t left = P.units - tile_u0;
     const int uv = left <= 0 ? 0 : (left < T::NU ? (int)left : T::NU);
-    float acc[G][8];
     if (uv > 0) {
       const uint32_t sbase = ring0 + (uint32_t)st * P.stage_bytes;
       const uint32_t kbase = sbase + (uint32_t)(j * T::NU * s_len) * (D * 2) + cl * 16;
       const uint32_t vbase = kbase + P.v_off;
       const uint32_t qbase = sbase + P.q_off + (uint32_t)(j * T::NU) * (G * D * 2) + cl * 16;
-      float q[G][8];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (ul < uv) w = lds128(qbase + (uint32_t)(ul * G + g) * (D * 2));
-        unpack8(w, q[g]);
-      }
       auto row_off = [&](int p) -> uint32_t {
-        const int r = p * T::RPP + r0;
+        const int r = r0 * T::NP + p;
         return (uint32_t)((r / SMAX) * s_len + (r % SMAX)) * (D * 2);
       };
       auto loadK = [&](int p) { return lds128(kbase + row_off(p)); };
       auto loadV = [&](int p) { return lds128(vbase + row_off(p)); };
-      attend_tile<D, SMAX, G>(q, loadK, loadV, s_len, uv, P.scale_log2, sc, lane, acc);
+      auto loadQ = [&](int u, int g) { return lds128(qbase + (uint32_t)(u * G + g) * (D * 2)); };
+      auto store = [&](int u, const float (&acc)[G][8]) {
+        if (u >= uv) return;
+        uint16_t* orow = P.O + (tile_u0 + u) * (G * D) + cl * 8;
+#pragma unroll
+        for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
+      };
+      attend_tile16<D, SMAX, G>(loadK, loadV, loadQ, store, s_len, uv, P.scale_log2, sc, lane);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8u * st);  // stage's shared reads are done
-    if (uv > 0 && ul < uv && OutputMap<D, SMAX, G>::writer(lane)) {
-      uint16_t* orow = P.O + (tile_u0 + ul) * (G * D) + cl * 8;
-#pragma unroll
-      for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
-    }
   }
 }
 

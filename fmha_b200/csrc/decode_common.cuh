@@ -25,7 +25,8 @@
 namespace fmha {
 
 constexpr unsigned kFullMask = 0xffffffffu;
-constexpr int kBulkThreads = 288;  // 1 producer warp + 8 consumer warps
+constexpr int kBulkMaxThreads = 544;  // 1 producer warp + up to 16 consumer warps
+constexpr int kBulkDefaultWarps = 16;  // consumer warps per CTA
 constexpr int kLdgThreads = 256;   // 8 warps
 constexpr int kHdrBytes = 1024;    // mbarriers + abort flag of the bulk kernel
 constexpr int kMaxStages = 48;
@@ -37,7 +38,12 @@ constexpr int kFlagStallProducer = 1;
 
 // Device error word (first error wins). Low byte: fmha_status_t value;
 // bits 8..15: the wait site that gave up.
-enum : unsigned { kSiteProducerEmpty = 1, kSiteConsumerFull = 2, kSiteDrain = 3 };
+enum : unsigned {
+  kSiteProducerEmpty = 1,
+  kSiteConsumerFull = 2,
+  kSiteDrain = 3,
+  kSiteConsumerIssued = 4
+};
 
 struct Params {
   const uint16_t* Q;
@@ -141,6 +147,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// Bounded wait until the producer has published `*issued > k` (chunk k's
+// copies and its `full` phase are armed). Same exit rules as mbar_wait.
+__device__ __forceinline__ bool wait_issued(volatile int* issued, int k, volatile int* abort_flag,
+                                            unsigned* err, unsigned long long timeout_ns) {
+  if (*issued > k) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    if (*issued > k) return true;
+    if ((it & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        report_device_error(err, 5u /* FMHA_ERR_DEVICE_TIMEOUT */, kSiteConsumerIssued);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -223,24 +249,29 @@ __device__ __forceinline__ uint4 pack8_f16(const float (&a)[8]) {
 // partner lane (xor `o`), so N values need N-1 shuffles instead of
 // N*log2(LPR). Afterwards lane cl holds the full sum of index
 // cl >> HOLD_SHIFT (replicated over the low HOLD_SHIFT lane bits).
-template <int N, int LPR>
-__device__ __forceinline__ float reduce_scatter(float (&v)[N], int cl) {
+template <int N, int O, int M>
+__device__ __forceinline__ void reduce_scatter_step(float (&v)[M], int cl) {
+  if constexpr (O >= 1) {
+    if constexpr (N > 1) {
+      constexpr int H = N / 2;
+      const bool upper = (cl & O) != 0;
 #pragma unroll
-  for (int o = LPR / 2, n = N; o >= 1; o >>= 1) {
-    if (n > 1) {
-      const int half = n / 2;
-      const bool upper = (cl & o) != 0;
-#pragma unroll
-      for (int i = 0; i < half; ++i) {
-        const float send = upper ? v[i] : v[i + half];
-        const float keep = upper ? v[i + half] : v[i];
-        v[i] = keep + __shfl_xor_sync(kFullMask, send, o);
+      for (int i = 0; i < H; ++i) {
+        const float send = upper ? v[i] : v[i + H];
+        const float keep = upper ? v[i + H] : v[i];
+        v[i] = keep + __shfl_xor_sync(kFullMask, send, O);
       }
-      n = half;
+      reduce_scatter_step<H, O / 2>(v, cl);
     } else {
-      v[0] += __shfl_xor_sync(kFullMask, v[0], o);
+      v[0] += __shfl_xor_sync(kFullMask, v[0], O);
+      reduce_scatter_step<1, O / 2>(v, cl);
     }
   }
+}
+
+template <int N, int LPR>
+__device__ __forceinline__ float reduce_scatter(float (&v)[N], int cl) {
+  reduce_scatter_step<N, LPR / 2>(v, cl);
   return v[0];
 }
 
@@ -323,6 +354,145 @@ __device__ __forceinline__ void attend_tile(const float (&q)[G][8], LoadK loadK,
     for (int g = 0; g < G; ++g)
 #pragma unroll
       for (int c = 0; c < 8; ++c) acc[g][c] += __shfl_xor_sync(kFullMask, acc[g][c], 16);
+  }
+}
+
+// ----------------------------------------------------------------------
+// 16-row tiles (bulk family). A tile is always 16 K/V rows = NU = 16/SMAX
+// units, whatever seqlen_kv is, so the score reduction, the softmax and their
+// warp synchronisations are paid once per 16 rows instead of once per unit.
+// Lane l (row group r0 = l / LPR, column block cl = l % LPR) owns rows
+// r0*NP + p, p = 0..NP-1 (D=256: all 16 rows; D=128: half of them). Its rows
+// fall into LU "slots" of SPL consecutive rows of one unit; only when a unit
+// is longer than a lane's rows (D=128, SMAX=16) do the two row groups share a
+// unit and sum their P.V partials with one xor-16 shuffle.
+template <int D, int SMAX, int G>
+struct Tile16 {
+  static_assert(D == 128 || D == 256, "head_dim");
+  static constexpr int LPR = D / 8;
+  static constexpr int RPP = 32 / LPR;
+  static constexpr int ROWS = 16;
+  static constexpr int NP = ROWS / RPP;                 // rows per lane
+  static constexpr int NU = ROWS / SMAX;                // units per tile
+  static constexpr int SPL = NP < SMAX ? NP : SMAX;     // rows per slot
+  static constexpr int LU = NP / SPL;                   // slots per lane
+  static constexpr bool CROSS = SMAX > NP;              // unit spans both row groups
+  static constexpr int GB = G < 32 / NP ? G : 32 / NP;  // query heads per score pass
+  static constexpr int LOG_LPR = LPR == 32 ? 5 : 4;
+  static constexpr int LOG_NP = NP == 16 ? 4 : 3;
+  static constexpr int HOLD_SHIFT = LOG_LPR - LOG_NP;
+  static constexpr int SC = G * ROWS;
+  static_assert(G % GB == 0, "GB");
+};
+
+__device__ __forceinline__ float dot8f(const float (&q)[8], const float (&k)[8]) {
+  float a = q[0] * k[0];
+#pragma unroll
+  for (int c = 1; c < 8; ++c) a = fmaf(q[c], k[c], a);
+  return a;
+}
+
+// One warp, one 16-row tile. loadK(p)/loadV(p): this lane's 16 bytes of its
+// row p (local index 0..NP-1); loadQ(u, g): its 16 bytes of query head g of
+// tile unit u; store(u, acc): called once per (slot, lane) with the lane's 8
+// output columns of every head of unit u -- the caller stores when
+// u < units_valid and writer() holds. Same math as attend_tile.
+template <int D, int SMAX, int G, class LoadK, class LoadV, class LoadQ, class Store>
+__device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ loadQ, Store store,
+                                              int s_len, int units_valid, float scale_log2,
+                                              float* sc, int lane) {
+  using T = Tile16<D, SMAX, G>;
+  const int r0 = lane / T::LPR;
+  const int cl = lane % T::LPR;
+  auto row_ok = [&](int p) {
+    const int r = r0 * T::NP + p;
+    return (r % SMAX) < s_len && (r / SMAX) < units_valid;
+  };
+  auto slot_unit = [&](int us) { return (r0 * T::NP + us * T::SPL) / SMAX; };
+
+  __syncwarp();
+#pragma unroll
+  for (int gb = 0; gb < G; gb += T::GB) {
+    float v[T::GB][T::NP];
+#pragma unroll
+    for (int us = 0; us < T::LU; ++us) {
+      const int u = slot_unit(us);
+      float q[T::GB][8];
+#pragma unroll
+      for (int g = 0; g < T::GB; ++g) {
+        if (u < units_valid) {
+          unpack8(loadQ(u, gb + g), q[g]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) q[g][c] = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < T::SPL; ++i) {
+        const int p = us * T::SPL + i;
+        if (row_ok(p)) {
+          float kf[8];
+          unpack8(loadK(p), kf);
+#pragma unroll
+          for (int g = 0; g < T::GB; ++g) v[g][p] = dot8f(q[g], kf);
+        } else {
+#pragma unroll
+          for (int g = 0; g < T::GB; ++g) v[g][p] = 0.0f;
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < T::GB; ++g) {
+      const float s = reduce_scatter<T::NP, T::LPR>(v[g], cl);
+      const int pi = cl >> T::HOLD_SHIFT;
+      if ((cl & ((1 << T::HOLD_SHIFT) - 1)) == 0)
+        sc[(gb + g) * T::ROWS + r0 * T::NP + pi] = row_ok(pi) ? s * scale_log2 : -INFINITY;
+    }
+  }
+  __syncwarp();
+
+#pragma unroll
+  for (int base = 0; base < T::SC; base += 32) {
+    const int e = base + lane;
+    const float x = e < T::SC ? sc[e] : -INFINITY;
+    float m = x;
+#pragma unroll
+    for (int o = 1; o < SMAX; o <<= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
+    const float ex = (m == -INFINITY) ? 0.0f : exp2f(x - m);
+    float sum = ex;
+#pragma unroll
+    for (int o = 1; o < SMAX; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
+    if (e < T::SC) sc[e] = sum > 0.0f ? ex / sum : 0.0f;
+  }
+  __syncwarp();
+
+#pragma unroll
+  for (int us = 0; us < T::LU; ++us) {
+    float acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[g][c] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < T::SPL; ++i) {
+      const int p = us * T::SPL + i;
+      if (!row_ok(p)) continue;
+      float vf[8];
+      unpack8(loadV(p), vf);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pr = sc[g * T::ROWS + r0 * T::NP + p];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[g][c] = fmaf(pr, vf[c], acc[g][c]);
+      }
+    }
+    if constexpr (T::CROSS) {
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[g][c] += __shfl_xor_sync(kFullMask, acc[g][c], 16);
+    }
+    if (!T::CROSS || r0 == 0) store(slot_unit(us), acc);
   }
 }
 

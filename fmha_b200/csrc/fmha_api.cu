@@ -143,10 +143,12 @@ fmha_status_t launch_bulk(Params P, int d, int smax, int g, const DeviceInfo& de
                           cudaStream_t stream) {
   KernelFn fn = d == 128 ? bulk_kernel_d128(smax, g) : bulk_kernel_d256(smax, g);
   if (!fn) return FMHA_ERR_UNSUPPORTED;
-  const int rpp = rows_per_access(d);
-  const int rows = smax > rpp ? smax : rpp;
+  const int rows = 16;  // Tile16: every tile is 16 K/V rows
   const int nu = rows / smax;
   const int s = P.s_len;
+  int ncw = env_int("FMHA_BULK_WARPS", kBulkDefaultWarps);
+  if (ncw < 1) ncw = 1;
+  if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
   const int64_t tile_bytes = (int64_t)nu * (2LL * s * d * 2 + (int64_t)g * d * 2);
   const int target = env_int("FMHA_STAGE_BYTES", 32768);
   int ct = (int)(target / tile_bytes);
@@ -156,7 +158,7 @@ fmha_status_t launch_bulk(Params P, int d, int smax, int g, const DeviceInfo& de
   const uint32_t qb = (uint32_t)cu * g * d * 2;
   const uint32_t stage = (2 * kb + qb + 127u) & ~127u;
   const uint32_t sc_off = kHdrBytes;
-  const uint32_t sc_bytes = (uint32_t)(kBulkThreads / 32 - 1) * g * rows * 4;
+  const uint32_t sc_bytes = (uint32_t)ncw * g * rows * 4;
   const uint32_t ring_off = (sc_off + sc_bytes + 1023u) & ~1023u;
   // One CTA per SM by default (the whole shared memory); FMHA_BULK_CTAS_PER_SM
   // splits the SM's 228 KiB (1 KiB reserved per CTA) between several rings.
@@ -182,7 +184,7 @@ fmha_status_t launch_bulk(Params P, int d, int smax, int g, const DeviceInfo& de
   if (st != FMHA_OK) return st;
   int grid = dev.sms * ctas_per_sm;
   if (grid > P.chunks) grid = P.chunks;
-  fn<<<grid, kBulkThreads, smem, stream>>>(P);
+  fn<<<grid, 32 * (1 + ncw), smem, stream>>>(P);
   return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
 }
 

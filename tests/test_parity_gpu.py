@@ -142,7 +142,7 @@ def test_device_timeout_is_reported_not_trapped(cuda, oracle):
     finally:
         lib.fmha_test_inject_stall(0)
     assert code & 0xff == fmha_b200.FMHA_ERR_DEVICE_TIMEOUT
-    assert (code >> 8) in (1, 2)
+    assert (code >> 8) in (1, 2, 4)
     ref32, _ = oracle.decode_bhsd(q, k, v, b, h, h, s, d)
     check_close(run_kernel(cuda, q, k, v, b, h, h, s, d), ref32)
     assert fmha_b200.device_error() == 0
