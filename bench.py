@@ -275,6 +275,10 @@ def main():
                     help="override the config's batch (small profiling cases only)")
     ap.add_argument("--sweep", action="store_true",
                     help="device-time lines for every config and variant (no e2e/cpu)")
+    ap.add_argument("--sweep-configs", default="",
+                    help="comma-separated config names for --sweep (default: all)")
+    ap.add_argument("--sweep-warps", default="8,16",
+                    help="bulk consumer-warp counts to try in --sweep")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -310,13 +314,18 @@ def main():
         return float(t.item())
 
     if args.sweep:
-        names = sorted(CONFIGS)
+        names = [x for x in args.sweep_configs.split(",") if x] or sorted(CONFIGS)
+        trials = [("ldg", None)] + [("bulk", int(w)) for w in args.sweep_warps.split(",") if w]
         for name in names:
-            for var in ("bulk", "ldg"):
+            for var, warps in trials:
+                if warps is not None:
+                    os.environ["FMHA_BULK_WARPS"] = str(warps)
                 r = time_config(torch, fmha_b200, CONFIGS[name], world, rank, args, var, barrier,
                                 max_over_ranks, dev, clocks=False)
                 if rank == 0:
-                    print(json.dumps({"sweep": name, "variant": var, **r}), flush=True)
+                    print(json.dumps({"sweep": name, "variant": var, "warps": warps, **r}),
+                          flush=True)
+        os.environ.pop("FMHA_BULK_WARPS", None)
         return 0
 
     cfg = CONFIGS[args.config]
@@ -363,9 +372,8 @@ def main():
 
 
 def shard(b_all, world, rank):
-    lo = b_all * rank // world
-    hi = b_all * (rank + 1) // world
-    return lo, hi
+    from fmha_b200.multi import shard_rows
+    return shard_rows(b_all, world, rank)
 
 
 def alloc_inputs(torch, fmha_b200, cfg, lo, hi, dev):

@@ -81,7 +81,7 @@ def build_lib(force: bool = False, verbose: bool = False) -> str:
                     sys.stderr.write(log)
     objs = [j[1] for j in _objects()]
     if force or _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs
         subprocess.check_call(cmd)
     return LIB
 
@@ -92,7 +92,7 @@ def build_host(force: bool = False) -> str | None:
         return None
     os.makedirs(os.path.dirname(HOST_BIN), exist_ok=True)
     if force or _stale(HOST_BIN, [src, LIB] + _headers()):
-        cmd = [nvcc(), "-O2", "-std=c++17", "-Xcompiler", "-fopenmp",
+        cmd = [nvcc()] + ARCH + ["-O2", "-std=c++17", "-cudart", "static", "-Xcompiler", "-fopenmp",
                "-I" + os.path.join(ROOT, "include"), src, "-o", HOST_BIN,
                "-L" + PKG, "-lfmha_b200", "-Xlinker", "-rpath=$ORIGIN/..", "-lgomp"]
         subprocess.check_call(cmd)

@@ -113,13 +113,28 @@ int smax_for(int s) {
 
 int rows_per_access(int d) { return 256 / d; }
 
-// Per-shape default family. Filled from B200 measurements (bench.py
-// --sweep); the bulk family is the default until a shape measures better
-// with ldg.
-int auto_variant(int /*d*/, int /*s*/, int /*g*/) {
+// Per-shape default: kernel family and bulk consumer-warp count, from a B200
+// sweep (bench.py --sweep, batch 30720, 100 calls per point). The ldg family
+// wins where one unit already fills a 16-row tile with 512-byte rows
+// (D=256, S=16, one query head per kv head) and for D=128, S=1; elsewhere the
+// bulk ring wins, with ~10 consumer warps for 8-16 row units (leaving ring
+// stages for copies in flight) and 16 for short units (more tiles per stage).
+// FMHA_VARIANT (1 bulk, 2 ldg) and FMHA_BULK_WARPS override the table.
+struct Choice {
+  int variant;
+  int warps;
+};
+
+Choice auto_choice(int d, int smax, int g) {
   static const int forced = env_int("FMHA_VARIANT", 0);
-  if (forced == FMHA_VARIANT_BULK || forced == FMHA_VARIANT_LDG) return forced;
-  return FMHA_VARIANT_BULK;
+  Choice c{FMHA_VARIANT_BULK, 16};
+  if (d == 256 && smax == 16 && g == 1) c = {FMHA_VARIANT_LDG, 0};
+  else if (d == 128 && smax == 1 && g == 1) c = {FMHA_VARIANT_LDG, 0};
+  else if (smax >= 8) c = {FMHA_VARIANT_BULK, 10};
+  else if (d == 128 && smax == 4) c = {FMHA_VARIANT_BULK, 8};
+  if (forced == FMHA_VARIANT_BULK || forced == FMHA_VARIANT_LDG) c.variant = forced;
+  if (c.warps == 0) c.warps = 10;
+  return c;
 }
 
 fmha_status_t check_args(const void* Q, const void* K, const void* V, void* O, int batch,
@@ -139,14 +154,14 @@ fmha_status_t check_args(const void* Q, const void* K, const void* V, void* O, i
   return FMHA_OK;
 }
 
-fmha_status_t launch_bulk(Params P, int d, int smax, int g, const DeviceInfo& dev,
+fmha_status_t launch_bulk(Params P, int d, int smax, int g, int warps, const DeviceInfo& dev,
                           cudaStream_t stream) {
   KernelFn fn = d == 128 ? bulk_kernel_d128(smax, g) : bulk_kernel_d256(smax, g);
   if (!fn) return FMHA_ERR_UNSUPPORTED;
   const int rows = 16;  // Tile16: every tile is 16 K/V rows
   const int nu = rows / smax;
   const int s = P.s_len;
-  int ncw = env_int("FMHA_BULK_WARPS", kBulkDefaultWarps);
+  int ncw = env_int("FMHA_BULK_WARPS", warps > 0 ? warps : kBulkDefaultWarps);
   if (ncw < 1) ncw = 1;
   if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
   const int64_t tile_bytes = (int64_t)nu * (2LL * s * d * 2 + (int64_t)g * d * 2);
@@ -307,10 +322,11 @@ fmha_status_t fmha_forward_variant(const void* Q, const void* K, const void* V, 
   P.units = (int64_t)batch * num_heads_kv;
   P.s_len = seqlen_kv;
   P.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
-  if (variant == FMHA_VARIANT_AUTO) variant = auto_variant(head_dim, seqlen_kv, g);
+  const Choice c = auto_choice(head_dim, smax, g);
+  if (variant == FMHA_VARIANT_AUTO) variant = c.variant;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return variant == FMHA_VARIANT_LDG ? launch_ldg(P, head_dim, smax, g, dev, s)
-                                     : launch_bulk(P, head_dim, smax, g, dev, s);
+                                     : launch_bulk(P, head_dim, smax, g, c.warps, dev, s);
 }
 
 fmha_status_t fmha_forward(const void* Q, const void* K, const void* V, void* O, int batch,

@@ -1,0 +1,419 @@
+// fmha_host.cpp -- benchmark / validation host for libfmha_b200 (C ABI,
+// include/fmha.h). B200 counterpart of the reference's host program
+// (HGLiu1998/fmha fmha_host.cpp): same config table and argv index
+// (fmha_host.cpp:477-533), same warm-up/iteration defaults (5/20,
+// fmha_host.cpp:298), same printed metrics (ms/iter, iter/s, TFLOPS, us per
+// head, GB/s; fmha_host.cpp:397-432) and the same post-run validation
+// (fmha_host.cpp:434-445), with these differences:
+//   * K/V use the [B,Hkv,S,D] layout with a fixed seqlen_kv (default 16),
+//     inputs come from the library's seeded counter-based generator
+//     (fmha_fill_normal_bf16) instead of unseeded U[-1,1];
+//   * --gpus N splits the batch into N contiguous shards, one host thread per
+//     GPU, started together on a host barrier; the aggregate bandwidth is
+//     total bytes / slowest GPU's device time (no collective: shards are
+//     independent and outputs stay on their GPUs);
+//   * validation recomputes a deterministic sample of batch rows on the CPU
+//     (fp32 softmax, the reference's arithmetic order, fmha_host.cpp:179-243)
+//     with OpenMP over the host cores, checks max|o-r| <= 2e-3 or <= 1e-2|r|,
+//     and reports the CPU time per row as the CPU baseline.
+//
+// Usage: fmha_host [config_index] [--all] [--gpus N] [--iters N] [--warmups N]
+//                  [--seqlen S] [--seed S] [--variant auto|bulk|ldg]
+//                  [--validate-rows N] [--json]
+#include <cuda_runtime.h>
+#include <omp.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <condition_variable>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "fmha.h"
+
+namespace {
+
+#define CUDA_CHECK(cmd)                                                                      \
+  do {                                                                                       \
+    cudaError_t e_ = (cmd);                                                                  \
+    if (e_ != cudaSuccess) {                                                                 \
+      std::fprintf(stderr, "CUDA error %s at %s:%d\n", cudaGetErrorString(e_), __FILE__,    \
+                   __LINE__);                                                                \
+      std::exit(EXIT_FAILURE);                                                               \
+    }                                                                                        \
+  } while (0)
+
+#define FMHA_CHECK(cmd)                                                                      \
+  do {                                                                                       \
+    fmha_status_t s_ = (cmd);                                                                \
+    if (s_ != FMHA_OK) {                                                                     \
+      std::fprintf(stderr, "fmha error %s at %s:%d\n", fmha_status_string(s_), __FILE__,    \
+                   __LINE__);                                                                \
+      std::exit(EXIT_FAILURE);                                                               \
+    }                                                                                        \
+  } while (0)
+
+struct Config {
+  int batch, num_heads_q, num_heads_kv, head_dim;
+  const char* note;
+};
+
+// Index 0..4: the reference's table (fmha_host.cpp:511-517). 5: GQA 32/16.
+const Config kConfigs[] = {
+    {10, 16, 16, 128, "testing"},
+    {30720, 16, 16, 128, "config 0: 16 heads, dim 128"},
+    {30720, 16, 16, 256, "config 1: 16 heads, dim 256"},
+    {30720, 32, 32, 128, "config 2: 32 heads, dim 128"},
+    {30720, 32, 32, 256, "config 3: 32 heads, dim 256"},
+    {30720, 32, 16, 256, "GQA: 32 query heads over 16 kv heads, dim 256"},
+};
+constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
+
+struct Options {
+  int config = -1;
+  int gpus = 1;
+  int iters = 20;
+  int warmups = 5;
+  int seqlen = 16;
+  uint64_t seed = 0;
+  int variant = FMHA_VARIANT_AUTO;
+  int validate_rows = 64;
+  bool json = false;
+};
+
+// ------------------------------------------------------------ host generator
+// Same values as fmha_fill_normal_bf16 (splitmix64 of (seed, tensor, index),
+// Irwin-Hall sum of twelve 16-bit uniforms, bf16 RNE).
+uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+uint16_t f32_to_bf16(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+float bf16_to_f32(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+float f16_to_f32(uint16_t h) {
+  const uint32_t s = (h >> 15) & 1, e = (h >> 10) & 31, m = h & 1023;
+  float v;
+  if (e == 0) v = std::ldexp((float)m, -24);
+  else if (e == 31) v = m ? NAN : INFINITY;
+  else v = std::ldexp((float)(m | 1024), (int)e - 25);
+  return s ? -v : v;
+}
+
+void gen_bf16(uint16_t* out, int64_t n, uint64_t seed, uint32_t tensor, int64_t offset) {
+  const uint64_t key = mix64(seed ^ mix64(((uint64_t)tensor << 32) | 0x5bd1e995u));
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t e = (uint64_t)(offset + i);
+    int64_t t = 0;
+    for (int j = 0; j < 3; ++j) {
+      const uint64_t h = mix64(key + e * 3u + (uint64_t)j);
+      t += (int64_t)(h & 0xffffu) + (int64_t)((h >> 16) & 0xffffu) +
+           (int64_t)((h >> 32) & 0xffffu) + (int64_t)(h >> 48);
+    }
+    out[i] = f32_to_bf16((float)(2 * t + 12 - 12 * 65536) * (1.0f / 131072.0f));
+  }
+}
+
+// ------------------------------------------------------------ CPU check
+// One batch row, all heads: fp32 softmax(q.k^T/sqrt(D)) v in the reference's
+// operation order (fmha_host.cpp:179-243), P kept in fp32.
+void cpu_row(const uint16_t* q, const uint16_t* k, const uint16_t* v, int hq, int hkv, int s,
+             int d, float* out) {
+  const int g = hq / hkv;
+  for (int h = 0; h < hq; ++h) {
+    const int kvh = h / g;
+    const uint16_t* qh = q + (int64_t)h * d;
+    const uint16_t* kh = k + (int64_t)kvh * s * d;
+    const uint16_t* vh = v + (int64_t)kvh * s * d;
+    float sc[16];
+    for (int j = 0; j < s; ++j) {
+      float acc = 0.f;
+      for (int c = 0; c < d; ++c) acc += bf16_to_f32(qh[c]) * bf16_to_f32(kh[(int64_t)j * d + c]);
+      sc[j] = acc * (1.0f / std::sqrt((float)d));
+    }
+    float mx = -INFINITY;
+    for (int j = 0; j < s; ++j) mx = std::max(mx, sc[j]);
+    float sum = 0.f;
+    for (int j = 0; j < s; ++j) sum += std::exp(sc[j] - mx);
+    for (int j = 0; j < s; ++j) sc[j] = std::exp(sc[j] - mx) / sum;
+    for (int c = 0; c < d; ++c) {
+      float acc = 0.f;
+      for (int j = 0; j < s; ++j) acc += sc[j] * bf16_to_f32(vh[(int64_t)j * d + c]);
+      out[(int64_t)h * d + c] = acc;
+    }
+  }
+}
+
+// ------------------------------------------------------------ per-GPU shard
+
+struct HostBarrier {
+  std::mutex mu;
+  std::condition_variable cv;
+  int count = 0, gen = 0, n = 0;
+  void wait() {
+    std::unique_lock<std::mutex> lk(mu);
+    const int g = gen;
+    if (++count == n) {
+      count = 0;
+      ++gen;
+      cv.notify_all();
+    } else {
+      cv.wait(lk, [&] { return gen != g; });
+    }
+  }
+};
+
+struct ShardResult {
+  double ms_per_iter = 0;
+  int64_t rows_checked = 0;
+  int64_t bad = 0;
+  double max_abs = 0, max_rel = 0;
+  double cpu_sec = 0;
+  int device_error = 0;
+};
+
+void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64_t rows,
+               HostBarrier& bar, ShardResult& res) {
+  CUDA_CHECK(cudaSetDevice(gpu));
+  const int hq = cfg.num_heads_q, hkv = cfg.num_heads_kv, d = cfg.head_dim, s = o.seqlen;
+  const int64_t nq = rows * hq * d, nkv = rows * hkv * s * d;
+  void *dQ, *dK, *dV, *dO;
+  CUDA_CHECK(cudaMalloc(&dQ, nq * 2));
+  CUDA_CHECK(cudaMalloc(&dK, nkv * 2));
+  CUDA_CHECK(cudaMalloc(&dV, nkv * 2));
+  CUDA_CHECK(cudaMalloc(&dO, nq * 2));
+  cudaStream_t st;
+  CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  fmha_stream_t fs = reinterpret_cast<fmha_stream_t>(st);
+  FMHA_CHECK(fmha_fill_normal_bf16(dQ, nq, o.seed, 1, row0 * hq * d, fs));
+  FMHA_CHECK(fmha_fill_normal_bf16(dK, nkv, o.seed, 2, row0 * hkv * s * d, fs));
+  FMHA_CHECK(fmha_fill_normal_bf16(dV, nkv, o.seed, 3, row0 * hkv * s * d, fs));
+  CUDA_CHECK(cudaMemsetAsync(dO, 0, nq * 2, st));
+  auto launch = [&] {
+    FMHA_CHECK(fmha_forward_variant(dQ, dK, dV, dO, (int)rows, hq, hkv, s, d, o.variant, fs));
+  };
+  for (int i = 0; i < o.warmups; ++i) launch();
+  CUDA_CHECK(cudaStreamSynchronize(st));
+  cudaEvent_t e0, e1;
+  CUDA_CHECK(cudaEventCreate(&e0));
+  CUDA_CHECK(cudaEventCreate(&e1));
+  bar.wait();  // every GPU starts its timed loop together
+  CUDA_CHECK(cudaEventRecord(e0, st));
+  for (int i = 0; i < o.iters; ++i) launch();
+  CUDA_CHECK(cudaEventRecord(e1, st));
+  CUDA_CHECK(cudaEventSynchronize(e1));
+  float ms = 0;
+  CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+  res.ms_per_iter = ms / o.iters;
+  FMHA_CHECK(fmha_device_error(&res.device_error));
+
+  // Validation: a deterministic sample of this shard's rows (all if few).
+  std::vector<uint16_t> hO(nq);
+  CUDA_CHECK(cudaMemcpy(hO.data(), dO, nq * 2, cudaMemcpyDeviceToHost));
+  std::vector<int64_t> pick;
+  if (o.validate_rows <= 0 || rows <= o.validate_rows) {
+    for (int64_t r = 0; r < rows; ++r) pick.push_back(r);
+  } else {
+    for (int i = 0; i < o.validate_rows; ++i)
+      pick.push_back((int64_t)((mix64((uint64_t)i + 977) % (uint64_t)rows)));
+    pick.push_back(0);
+    pick.push_back(rows - 1);
+  }
+  int64_t bad = 0;
+  double max_abs = 0, max_rel = 0;
+  const auto t0 = std::chrono::steady_clock::now();
+#pragma omp parallel for schedule(dynamic) reduction(+ : bad) reduction(max : max_abs, max_rel)
+  for (size_t i = 0; i < pick.size(); ++i) {
+    const int64_t r = pick[i], gr = row0 + r;
+    std::vector<uint16_t> q(hq * d), k((int64_t)hkv * s * d), v((int64_t)hkv * s * d);
+    gen_bf16(q.data(), hq * d, o.seed, 1, gr * hq * d);
+    gen_bf16(k.data(), (int64_t)hkv * s * d, o.seed, 2, gr * hkv * s * d);
+    gen_bf16(v.data(), (int64_t)hkv * s * d, o.seed, 3, gr * hkv * s * d);
+    std::vector<float> ref((int64_t)hq * d);
+    cpu_row(q.data(), k.data(), v.data(), hq, hkv, s, d, ref.data());
+    for (int64_t c = 0; c < (int64_t)hq * d; ++c) {
+      const double got = f16_to_f32(hO[r * hq * d + c]);
+      const double err = std::fabs(got - ref[c]);
+      if (!(err <= 2e-3 || err <= 1e-2 * std::fabs(ref[c]))) ++bad;
+      max_abs = std::max(max_abs, err);
+      if (std::fabs(ref[c]) >= 0.2) max_rel = std::max(max_rel, err / std::fabs(ref[c]));
+    }
+  }
+  res.cpu_sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  res.rows_checked = (int64_t)pick.size();
+  res.bad = bad;
+  res.max_abs = max_abs;
+  res.max_rel = max_rel;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaStreamDestroy(st);
+  cudaFree(dQ);
+  cudaFree(dK);
+  cudaFree(dV);
+  cudaFree(dO);
+}
+
+bool run_config(int idx, const Options& o) {
+  const Config& cfg = kConfigs[idx];
+  const int hq = cfg.num_heads_q, hkv = cfg.num_heads_kv, d = cfg.head_dim, s = o.seqlen;
+  const int n = std::max(1, std::min(o.gpus, cfg.batch));
+  std::vector<ShardResult> res(n);
+  std::vector<std::thread> th;
+  HostBarrier bar;
+  bar.n = n;
+  for (int g = 0; g < n; ++g) {
+    const int64_t r0 = (int64_t)cfg.batch * g / n, r1 = (int64_t)cfg.batch * (g + 1) / n;
+    th.emplace_back(run_shard, g, std::cref(cfg), std::cref(o), r0, r1 - r0, std::ref(bar),
+                    std::ref(res[g]));
+  }
+  for (auto& t : th) t.join();
+
+  double ms = 0, cpu_sec = 0, max_abs = 0, max_rel = 0;
+  int64_t bad = 0, checked = 0;
+  int dev_err = 0;
+  for (auto& r : res) {
+    ms = std::max(ms, r.ms_per_iter);
+    bad += r.bad;
+    checked += r.rows_checked;
+    cpu_sec += r.cpu_sec;
+    max_abs = std::max(max_abs, r.max_abs);
+    max_rel = std::max(max_rel, r.max_rel);
+    dev_err |= r.device_error;
+  }
+  const double b = cfg.batch;
+  // Byte and flop formulas of fmha_host.cpp:413-414,428-431.
+  const double bytes = 2.0 * b * hq * d + 4.0 * b * hkv * s * d + 2.0 * b * hq * d;
+  const double flops = 4.0 * b * hq * s * d;
+  const double gbs = bytes / (ms * 1e-3) / 1e9;
+  const double cpu_ms_per_row = checked ? cpu_sec * 1e3 / checked * n : 0;  // per-thread-set
+  const int threads = omp_get_max_threads();
+  const bool ok = bad == 0 && dev_err == 0;
+  if (o.json) {
+    std::printf(
+        "{\"config\": %d, \"note\": \"%s\", \"batch\": %d, \"num_heads_q\": %d, "
+        "\"num_heads_kv\": %d, \"seqlen_kv\": %d, \"head_dim\": %d, \"gpus\": %d, "
+        "\"us_per_call\": %.3f, \"gbs\": %.1f, \"tflops\": %.3f, \"rows_checked\": %lld, "
+        "\"bad\": %lld, \"max_abs_err\": %.3e, \"max_rel_err\": %.3e, \"cpu_ms_per_row\": %.4f, "
+        "\"cpu_threads\": %d, \"device_error\": %d, \"passed\": %s}\n",
+        idx, cfg.note, cfg.batch, hq, hkv, s, d, n, ms * 1e3, gbs, flops / (ms * 1e-3) / 1e12,
+        (long long)checked, (long long)bad, max_abs, max_rel, cpu_ms_per_row, threads, dev_err,
+        ok ? "true" : "false");
+  } else {
+    std::printf("\n=== Configuration %d (%s) ===\n", idx, cfg.note);
+    std::printf("  Batch %d, heads Q %d, heads KV %d (%s), seqlen_q 1, seqlen_kv %d, head_dim %d\n",
+                cfg.batch, hq, hkv, hq == hkv ? "MHA" : "GQA", s, d);
+    std::printf("  Layout Q/O [B,H,1,D], K/V [B,Hkv,S,D]; bf16 in, fp32 softmax, fp16 out\n");
+    std::printf("  GPUs %d (batch shards of ~%d rows, no collective)\n", n, cfg.batch / n);
+    std::printf("Average time:  %.4f ms per iteration (slowest GPU)\n", ms);
+    std::printf("Throughput:    %.1f iter/s\n", 1000.0 / ms);
+    std::printf("Performance:   %.3f TFLOPS\n", flops / (ms * 1e-3) / 1e12);
+    std::printf("Per-head latency: %.6f us\n", ms * 1e3 / (b * hq));
+    std::printf("Memory bandwidth: %.1f GB/s (algorithmic bytes)\n", gbs);
+    std::printf("Validation: %lld rows on the CPU (%d OpenMP threads, %.3f ms/row): %s, "
+                "max abs err %.3e, max rel err %.3e\n",
+                (long long)checked, threads, cpu_ms_per_row, ok ? "passed" : "FAILED", max_abs,
+                max_rel);
+  }
+  return ok;
+}
+
+void usage() {
+  std::fprintf(stderr,
+               "usage: fmha_host [config_index 0..%d] [--all] [--gpus N] [--iters N] "
+               "[--warmups N] [--seqlen 1..16] [--seed S] [--variant auto|bulk|ldg] "
+               "[--validate-rows N] [--json]\n",
+               kNumConfigs - 1);
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  Options o;
+  bool all = false;
+  for (int i = 1; i < argc; ++i) {
+    std::string a = argv[i];
+    auto next = [&](const char* what) -> const char* {
+      if (i + 1 >= argc) {
+        std::fprintf(stderr, "missing value for %s\n", what);
+        std::exit(EXIT_FAILURE);
+      }
+      return argv[++i];
+    };
+    if (a == "--all") all = true;
+    else if (a == "--gpus") o.gpus = std::atoi(next("--gpus"));
+    else if (a == "--iters") o.iters = std::atoi(next("--iters"));
+    else if (a == "--warmups") o.warmups = std::atoi(next("--warmups"));
+    else if (a == "--seqlen") o.seqlen = std::atoi(next("--seqlen"));
+    else if (a == "--seed") o.seed = std::strtoull(next("--seed"), nullptr, 10);
+    else if (a == "--validate-rows") o.validate_rows = std::atoi(next("--validate-rows"));
+    else if (a == "--json") o.json = true;
+    else if (a == "--variant") {
+      std::string v = next("--variant");
+      o.variant = v == "bulk" ? FMHA_VARIANT_BULK : v == "ldg" ? FMHA_VARIANT_LDG
+                                                                : FMHA_VARIANT_AUTO;
+    } else if (a == "-h" || a == "--help") {
+      usage();
+      return 0;
+    } else if (!a.empty() && a[0] != '-') {
+      o.config = std::atoi(a.c_str());
+      if (o.config < 0 || o.config >= kNumConfigs) {
+        std::fprintf(stderr, "Error: config_index must be 0-%d\n", kNumConfigs - 1);
+        return EXIT_FAILURE;
+      }
+    } else {
+      usage();
+      return EXIT_FAILURE;
+    }
+  }
+  if (o.seqlen < 1 || o.seqlen > 16 || o.iters < 1 || o.warmups < 0 || o.gpus < 1) {
+    usage();
+    return EXIT_FAILURE;
+  }
+  int ndev = 0;
+  CUDA_CHECK(cudaGetDeviceCount(&ndev));
+  if (ndev == 0) {
+    std::fprintf(stderr, "Error: no CUDA devices found\n");
+    return EXIT_FAILURE;
+  }
+  if (o.gpus > ndev) {
+    std::fprintf(stderr, "Error: --gpus %d but only %d devices\n", o.gpus, ndev);
+    return EXIT_FAILURE;
+  }
+  cudaDeviceProp prop;
+  CUDA_CHECK(cudaGetDeviceProperties(&prop, 0));
+  if (!o.json) {
+    std::printf("Flash decode attention (fmha_b200) - CUDA benchmark\n");
+    std::printf("Using: %s (sm_%d%d, %d SMs, %.1f GB), %s\n", prop.name, prop.major, prop.minor,
+                prop.multiProcessorCount, prop.totalGlobalMem / 1e9, fmha_version());
+  }
+  bool ok = true;
+  if (o.config >= 0 && !all) {
+    ok = run_config(o.config, o);
+  } else {
+    for (int i = 0; i < kNumConfigs; ++i) ok = run_config(i, o) && ok;
+  }
+  if (!o.json) std::printf("\n%s\n", ok ? "Benchmark completed successfully!" : "FAILED");
+  return ok ? EXIT_SUCCESS : EXIT_FAILURE;
+}

@@ -1,0 +1,27 @@
+"""The C++ benchmark/validation host (fmha_b200/bin/fmha_host) on a GPU: the
+reference's "testing" config and a GQA config validate on the CPU and report
+sane metrics."""
+import json
+import os
+import subprocess
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+BIN = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "fmha_b200", "bin",
+                   "fmha_host")
+
+
+@pytest.mark.parametrize("args", [["0"], ["5", "--seqlen", "7", "--validate-rows", "16"],
+                                  ["0", "--variant", "bulk", "--seqlen", "1"]])
+def test_fmha_host_validates(cuda, args):
+    if not os.path.exists(BIN):
+        pytest.fail("fmha_host was not built (python -m fmha_b200.build)")
+    r = subprocess.run([BIN] + args + ["--json", "--iters", "5"], capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["passed"] and line["bad"] == 0 and line["device_error"] == 0
+    assert line["us_per_call"] > 0 and line["gbs"] > 0
+    assert line["max_abs_err"] <= 2e-3 or line["max_rel_err"] <= 1e-2

@@ -1,0 +1,65 @@
+"""Host-side logic of the batch-sharded multi-GPU path, on CPU with gloo
+(world size 2): shard ranges tile the batch, each rank's shard computed from
+its own regenerated inputs equals the same rows of the 1-process result, and
+the gathered output equals the full output bit for bit."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from fmha_b200.multi import make_shard, shard_rows
+
+
+@pytest.mark.parametrize("batch,world", [(30720, 8), (7, 2), (10, 3), (1, 4)])
+def test_shards_tile_the_batch(batch, world):
+    spans = [shard_rows(batch, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == batch
+    for (a, b), (c, _) in zip(spans, spans[1:]):
+        assert b == c and b >= a
+    assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
+    with pytest.raises(ValueError):
+        shard_rows(batch, world, world)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+SHAPE = (13, 32, 16, 5, 128)  # batch, hq, hkv, s, d
+
+
+def _worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from fmha_b200.multi import gather_output
+    from oracle import oracle as O
+    b, hq, hkv, s, d = SHAPE
+    sh = make_shard(b, hq, hkv, s, d, world, rank)
+    q, k, v = O.make_inputs_bhsd(sh.rows, hq, hkv, s, d, seed=9, batch_offset=sh.row0)
+    _, o16 = O.decode_bhsd(q, k, v, sh.rows, hq, hkv, s, d, want_f32=False)
+    full = gather_output(torch.from_numpy(o16.view(np.int16)), sh)
+    t = torch.tensor([float(rank + 1)])
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)  # max-over-ranks timing reduction
+    np.save(os.path.join(outdir, f"r{rank}.npy"), full.numpy())
+    np.save(os.path.join(outdir, f"m{rank}.npy"), t.numpy())
+    dist.destroy_process_group()
+
+
+def test_gloo_two_rank_shards_equal_single_process(tmp_path, oracle):
+    world = 2
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    b, hq, hkv, s, d = SHAPE
+    q, k, v = oracle.make_inputs_bhsd(b, hq, hkv, s, d, seed=9)
+    _, ref = oracle.decode_bhsd(q, k, v, b, hq, hkv, s, d, want_f32=False)
+    for r in range(world):
+        got = np.load(tmp_path / f"r{r}.npy").view(np.uint16)
+        assert np.array_equal(got, ref)
+        assert float(np.load(tmp_path / f"m{r}.npy")[0]) == world
