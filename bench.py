@@ -49,6 +49,11 @@ for _s in (1, 2, 4, 8, 16):
             CONFIGS.setdefault(f"h{_h}_d{_d}_s{_s}", (30720, _h, _h, _s, _d))
     CONFIGS.setdefault(f"gqa_32_16_d256_s{_s}", (30720, 32, 16, _s, 256))
 
+# The reference's own benchmark table (fmha_host.cpp:511-517): packed varlen
+# K/V with Poisson(4) seqlens in [2, 16] (seed 42) -> fmha_forward_varlen.
+VARLEN = {f"varlen_h{_h}_d{_d}": (30720, _h, _h, 16, _d) for _h in (16, 32) for _d in (128, 256)}
+CONFIGS.update(VARLEN)
+
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode-attn achieved HBM TB/s (algorithmic bytes / device time per call)"
@@ -320,8 +325,14 @@ def main():
             for var, warps in trials:
                 if warps is not None:
                     os.environ["FMHA_BULK_WARPS"] = str(warps)
-                r = time_config(torch, fmha_b200, CONFIGS[name], world, rank, args, var, barrier,
-                                max_over_ranks, dev, clocks=False)
+                if name in VARLEN:
+                    if var != "ldg":
+                        continue  # one varlen family
+                    r = time_varlen(torch, fmha_b200, CONFIGS[name], world, rank, args, barrier,
+                                    max_over_ranks, dev)
+                else:
+                    r = time_config(torch, fmha_b200, CONFIGS[name], world, rank, args, var,
+                                    barrier, max_over_ranks, dev, clocks=False)
                 if rank == 0:
                     print(json.dumps({"sweep": name, "variant": var, "warps": warps, **r}),
                           flush=True)
@@ -441,6 +452,56 @@ def time_config(torch, fmha_b200, cfg, world, rank, args, variant, barrier, max_
     torch.cuda.empty_cache()
     return {"value": round(total / (ms_max * 1e-3) / 1e12, 4), "ms_per_step": round(ms_max, 5),
             "kernel_ms": ms, "clocks": clk}
+
+
+def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev):
+    """fmha_forward_varlen on the reference's packed layout and seqlens; this
+    rank's batch shard. Bytes: Q + K + V (sum of seqlens) + O."""
+    import numpy as np
+    b_all, hq, hkv, max_s, d = cfg
+    sl_all = fmha_b200.seqlens_poisson(b_all, max_s, 42, 4.0)
+    lo, hi = shard(b_all, world, rank)
+    b = hi - lo
+    cu_all = np.concatenate([[0], np.cumsum(sl_all)]).astype(np.int64)
+    t0_row, t1_row = int(cu_all[lo]), int(cu_all[hi])
+    cu = torch.from_numpy((cu_all[lo:hi + 1] - t0_row).astype(np.int32)).to(dev)
+    Q = torch.empty(b * hq * d, dtype=torch.bfloat16, device=dev)
+    K = torch.empty((t1_row - t0_row) * hkv * d, dtype=torch.bfloat16, device=dev)
+    V = torch.empty_like(K)
+    fmha_b200.fill_normal_bf16(Q, 0, 1, lo * hq * d)
+    fmha_b200.fill_normal_bf16(K, 0, 2, t0_row * hkv * d)
+    fmha_b200.fill_normal_bf16(V, 0, 3, t0_row * hkv * d)
+    O = torch.empty(b * hq * d, dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def call():
+        st = fmha_b200.fmha_forward_varlen_ptr(Q, K, V, O, cu, b, hq, hkv, max_s, d, 0.0, sh)
+        if st != 0:
+            raise fmha_b200.FmhaError(st, "fmha_forward_varlen")
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        call()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    if fmha_b200.device_error() != 0:
+        raise RuntimeError("device error word set during the timed region")
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = max_over_ranks(ms)
+    total_rows = int(cu_all[-1])
+    total = 2 * b_all * hq * d + 4 * total_rows * hkv * d + 2 * b_all * hq * d
+    del Q, K, V, O
+    torch.cuda.empty_cache()
+    return {"value": round(total / (ms_max * 1e-3) / 1e12, 4), "ms_per_step": round(ms_max, 5),
+            "kernel_ms": ms, "clocks": None, "mean_seqlen": float(sl_all.mean())}
 
 
 def local_gpu_index(dev, r):

@@ -16,7 +16,7 @@ from ._lib import (FMHA_ERR_CUDA, FMHA_ERR_DEVICE_TIMEOUT, FMHA_ERR_INVALID_ARG,
                    FMHA_ERR_MISALIGNED, FMHA_ERR_UNSUPPORTED, FMHA_OK, VARIANTS, FmhaError,
                    check, load, status_string)
 
-__all__ = ["fmha_forward", "fmha_forward_ptr", "fill_normal_bf16", "device_error", "FmhaError",
+__all__ = ["fmha_forward", "fmha_forward_ptr", "fmha_forward_varlen_ptr", "seqlens_poisson", "fill_normal_bf16", "device_error", "FmhaError",
            "load", "version"]
 
 TENSOR_Q, TENSOR_K, TENSOR_V = 1, 2, 3
@@ -86,6 +86,24 @@ def fill_normal_bf16(t, seed: int, tensor_id: int, offset: int = 0, stream=None)
                                       _stream_handle(stream))
     check(st, "fmha_fill_normal_bf16")
     return t
+
+
+def seqlens_poisson(batch: int, max_seqlen_kv: int = 16, seed: int = 42, lam: float = 4.0):
+    """The reference benchmark's KV lengths (Poisson(4) in [2, 16], seed 42)."""
+    import numpy as np
+    out = np.empty(batch, dtype=np.int32)
+    check(load().fmha_seqlens_poisson(batch, max_seqlen_kv, seed, lam, out.ctypes.data),
+          "fmha_seqlens_poisson")
+    return out
+
+
+def fmha_forward_varlen_ptr(q, k, v, o, cu_seqlens, batch, num_heads_q, num_heads_kv,
+                            max_seqlen_kv, head_dim, softmax_scale=0.0, stream=None) -> int:
+    """Raw C call of fmha_forward_varlen; returns the status."""
+    return load().fmha_forward_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(cu_seqlens),
+                                      int(batch), int(num_heads_q), int(num_heads_kv),
+                                      int(max_seqlen_kv), int(head_dim), float(softmax_scale),
+                                      _stream_handle(stream))
 
 
 def device_error() -> int:

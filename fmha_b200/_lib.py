@@ -25,10 +25,12 @@ _vp, _i, _i64, _u64, _u32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctype
 SIGNATURES = {
     "fmha_forward": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "fmha_forward_variant": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "fmha_forward_varlen": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp]),
     "fmha_status_string": (ctypes.c_char_p, [_i]),
     "fmha_device_error": (_i, [ctypes.POINTER(_i)]),
     "fmha_fill_normal_bf16": (_i, [_vp, _i64, _u64, _u32, _i64, _vp]),
     "fmha_version": (ctypes.c_char_p, []),
+    "fmha_seqlens_poisson": (_i, [_i, _i, _u32, ctypes.c_double, _vp]),
     "fmha_test_inject_stall": (None, [_i]),
 }
 

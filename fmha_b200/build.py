@@ -51,7 +51,8 @@ def _stale(out: str, deps) -> bool:
 def _objects():
     objs = []
     for src, d in (("decode_bulk.cu", 128), ("decode_bulk.cu", 256),
-                   ("decode_ldg.cu", 128), ("decode_ldg.cu", 256)):
+                   ("decode_ldg.cu", 128), ("decode_ldg.cu", 256),
+                   ("decode_varlen.cu", 128), ("decode_varlen.cu", 256)):
         stem = src[:-3]
         objs.append((os.path.join(CSRC, src), os.path.join(BUILD, f"{stem}_d{d}.o"),
                      [f"-DFMHA_HEAD_DIM={d}"]))

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const P
       };
       auto loadK = [&](int p) { return lds128(kbase + row_off(p)); };
       auto loadV = [&](int p) { return lds128(vbase + row_off(p)); };
-      auto loadQ = [&](int u, int g) { return lds128(qbase + (uint32_t)(u * G + g) * (D * 2)); };
+      auto loadQ = [&](int, int u, int g) { return lds128(qbase + (uint32_t)(u * G + g) * (D * 2)); };
       auto store = [&](int u, const float (&acc)[G][8]) {
         if (u >= uv) return;
         uint16_t* orow = P.O + (tile_u0 + u) * (G * D) + cl * 8;

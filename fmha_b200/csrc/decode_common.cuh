@@ -393,8 +393,8 @@ __device__ __forceinline__ float dot8f(const float (&q)[8], const float (&k)[8])
 }
 
 // One warp, one 16-row tile. loadK(p)/loadV(p): this lane's 16 bytes of its
-// row p (local index 0..NP-1); loadQ(u, g): its 16 bytes of query head g of
-// tile unit u; store(u, acc): called once per (slot, lane) with the lane's 8
+// row p (local index 0..NP-1); loadQ(us, u, g): its 16 bytes of query head g
+// of tile unit u, the unit of the lane's slot us; store(u, acc): called once per (slot, lane) with the lane's 8
 // output columns of every head of unit u -- the caller stores when
 // u < units_valid and writer() holds. Same math as attend_tile.
 template <int D, int SMAX, int G, class LoadK, class LoadV, class LoadQ, class Store>
@@ -421,7 +421,7 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
 #pragma unroll
       for (int g = 0; g < T::GB; ++g) {
         if (u < units_valid) {
-          unpack8(loadQ(u, gb + g), q[g]);
+          unpack8(loadQ(us, u, gb + g), q[g]);
         } else {
 #pragma unroll
           for (int c = 0; c < 8; ++c) q[g][c] = 0.0f;
@@ -524,6 +524,24 @@ template <int D, int SMAX, int G, int TPI>
 __global__ void decode_ldg_kernel(const Params P);
 
 using KernelFn = void (*)(const Params);
+
+// Packed varlen layout (K/V [sum S_b, Hkv, D] + cu_seqlens_kv).
+struct VarlenParams {
+  const uint16_t* Q;
+  const uint16_t* K;
+  const uint16_t* V;
+  uint16_t* O;
+  const int32_t* cu_seqlens;  // [batch + 1], device
+  unsigned int* err;
+  int64_t batch;
+  int num_heads_kv;
+  int max_seqlen;     // rows longer than this are rejected (device error)
+  int tiles_per_row;  // 16-row tiles of a row of length max_seqlen
+  float scale_log2;   // log2(e) * softmax scale
+};
+using VarlenFn = void (*)(const VarlenParams);
+VarlenFn varlen_kernel_d128(int g);
+VarlenFn varlen_kernel_d256(int g);
 
 // Per-head_dim lookups of the instantiation for (SMAX, G); nullptr if absent.
 KernelFn bulk_kernel_d128(int smax, int g);

@@ -13,6 +13,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <random>
 #include <set>
 #include <utility>
 
@@ -329,6 +330,51 @@ fmha_status_t fmha_forward_variant(const void* Q, const void* K, const void* V, 
                                      : launch_bulk(P, head_dim, smax, g, c.warps, dev, s);
 }
 
+fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, void* O,
+                                  const int32_t* cu_seqlens_kv, int batch, int num_heads_q,
+                                  int num_heads_kv, int max_seqlen_kv, int head_dim,
+                                  float softmax_scale, fmha_stream_t stream) {
+  fmha_status_t st =
+      check_args(Q, K, V, O, batch, num_heads_q, num_heads_kv, max_seqlen_kv, head_dim);
+  if (st != FMHA_OK) return st;
+  if (batch > 0 && !cu_seqlens_kv) return FMHA_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(cu_seqlens_kv) & 3u) return FMHA_ERR_MISALIGNED;
+  if (!(softmax_scale >= 0.0f) || std::isinf(softmax_scale)) return FMHA_ERR_INVALID_ARG;
+  if (batch == 0) return FMHA_OK;
+  DeviceInfo dev;
+  st = device_info(&dev);
+  if (st != FMHA_OK) return st;
+  const int g = num_heads_q / num_heads_kv;
+  VarlenFn fn = head_dim == 128 ? varlen_kernel_d128(g) : varlen_kernel_d256(g);
+  if (!fn) return FMHA_ERR_UNSUPPORTED;
+  VarlenParams P;
+  std::memset(&P, 0, sizeof(P));
+  P.Q = static_cast<const uint16_t*>(Q);
+  P.K = static_cast<const uint16_t*>(K);
+  P.V = static_cast<const uint16_t*>(V);
+  P.O = static_cast<uint16_t*>(O);
+  P.cu_seqlens = cu_seqlens_kv;
+  P.err = dev.err;
+  P.batch = batch;
+  P.num_heads_kv = num_heads_kv;
+  P.max_seqlen = max_seqlen_kv;
+  const int smax = smax_for(max_seqlen_kv);
+  const int nu = 16 / smax;
+  P.tiles_per_row = (num_heads_kv + nu - 1) / nu;
+  const double scale = softmax_scale > 0.0f ? (double)softmax_scale
+                                            : 1.0 / std::sqrt((double)head_dim);
+  P.scale_log2 = (float)(1.4426950408889634 * scale);
+  int bps = 1;
+  st = blocks_per_sm(reinterpret_cast<KernelFn>(fn), kLdgThreads, &bps);
+  if (st != FMHA_OK) return st;
+  const int64_t tiles = (int64_t)batch * P.tiles_per_row;
+  int64_t grid = (int64_t)dev.sms * bps;
+  const int64_t need = (tiles + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
+  if (grid > need) grid = need;
+  fn<<<(unsigned)grid, kLdgThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+}
+
 fmha_status_t fmha_forward(const void* Q, const void* K, const void* V, void* O, int batch,
                            int num_heads_q, int num_heads_kv, int seqlen_kv, int head_dim,
                            fmha_stream_t stream) {
@@ -382,6 +428,22 @@ fmha_status_t fmha_fill_normal_bf16(void* dst, int64_t n, uint64_t seed, uint32_
 }
 
 void fmha_test_inject_stall(int on) { g_test_stall.store(on ? 1 : 0); }
+
+fmha_status_t fmha_seqlens_poisson(int batch, int max_seqlen_kv, uint32_t seed, double lambda,
+                                   int32_t* out) {
+  if (batch < 0 || max_seqlen_kv < 2 || !(lambda > 0.0) || (batch > 0 && !out))
+    return FMHA_ERR_INVALID_ARG;
+  std::mt19937 gen(seed);
+  std::poisson_distribution<int> dist(lambda);
+  for (int i = 0; i < batch; ++i) {
+    int len;
+    do {
+      len = dist(gen);
+    } while (len < 2 || len > max_seqlen_kv);
+    out[i] = len;
+  }
+  return FMHA_OK;
+}
 
 const char* fmha_version(void) { return "fmha_b200 0.1.0 sm_100a"; }
 

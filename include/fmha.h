@@ -17,7 +17,7 @@
  * (HGLiu1998/fmha fmha_mfma_4x4x4_kernel.hpp:370-389, called from
  * fmha_host.cpp:367,382,437). That helper takes a launch shape and a packed
  * varlen K/V layout; this ABI takes the [B,H,S,D] layout and chooses its own
- * launch shape. Its packed-layout form is fmha_forward_varlen().
+ * launch shape; fmha_forward_varlen() takes the reference's packed layout.
  *
  * Conventions shared by every entry point:
  *  - pointers are caller-owned device pointers, 16-byte aligned; the library
@@ -84,6 +84,27 @@ fmha_status_t fmha_forward_variant(const void* Q, const void* K, const void* V,
                                    int head_dim, int variant,
                                    fmha_stream_t stream);
 
+/*
+ * fmha_forward_varlen -- decode attention on the reference's packed varlen
+ * K/V layout:
+ *   Q [batch, num_heads_q, 1, head_dim]                 bf16
+ *   K [cu_seqlens_kv[batch], num_heads_kv, head_dim]    bf16 (rows of batch b
+ *   V [cu_seqlens_kv[batch], num_heads_kv, head_dim]    are cu[b] .. cu[b+1]-1)
+ *   O [batch, num_heads_q, 1, head_dim]                 fp16 (written)
+ *   cu_seqlens_kv [batch + 1] int32, device memory, cu[0] = 0, non-decreasing.
+ * Each row length cu[b+1]-cu[b] must lie in 0..max_seqlen_kv (max_seqlen_kv
+ * in 1..16); a longer row is skipped and reported through fmha_device_error
+ * (FMHA_ERR_INVALID_ARG), an empty row yields zeros. softmax_scale <= 0 means
+ * 1/sqrt(head_dim). Same grouping kvh = h / (Hq/Hkv) as fmha_forward.
+ * Replaces launch_fmha_mfma_4x4x4 with its own argument list
+ * (fmha_mfma_4x4x4_kernel.hpp:370-389; the layout of fmha_host.cpp:143-157).
+ */
+fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V,
+                                  void* O, const int32_t* cu_seqlens_kv,
+                                  int batch, int num_heads_q, int num_heads_kv,
+                                  int max_seqlen_kv, int head_dim,
+                                  float softmax_scale, fmha_stream_t stream);
+
 /* Human-readable name of a status code (static storage). Reference
  * counterpart: the HIP_CHECK error text (fmha_host.cpp:26-35). */
 const char* fmha_status_string(fmha_status_t status);
@@ -108,6 +129,17 @@ fmha_status_t fmha_device_error(int* code);
 fmha_status_t fmha_fill_normal_bf16(void* dst, int64_t n, uint64_t seed,
                                     uint32_t tensor_id, int64_t offset,
                                     fmha_stream_t stream);
+
+/*
+ * fmha_seqlens_poisson -- benchmark utility (host memory, no GPU): the
+ * reference benchmark's per-row KV lengths, drawn from Poisson(lambda) with a
+ * std::mt19937(seed) and redrawn until they lie in [2, max_seqlen_kv].
+ * Reference counterpart: FMHAConfig::generate_seqlens_kv
+ * (fmha_host.cpp:58-72), which uses seed 42 and lambda 4; with the same C++
+ * standard library the sequences are identical.
+ */
+fmha_status_t fmha_seqlens_poisson(int batch, int max_seqlen_kv, uint32_t seed,
+                                   double lambda, int32_t* out);
 
 /* Test hook for the device-side failure path: while `on` is non-zero every
  * fmha_forward* call runs the bulk kernel with its producer issuing no

@@ -2,6 +2,8 @@
 include/fmha.h declares, and rejects bad arguments before touching CUDA (so
 these calls need no GPU)."""
 import ctypes
+
+import numpy as np
 import os
 import re
 
@@ -91,3 +93,40 @@ def test_device_error_needs_pointer():
     lib = fmha_b200.load()
     assert lib.fmha_device_error(ctypes.cast(0, ctypes.POINTER(ctypes.c_int))) == \
         _lib.FMHA_ERR_INVALID_ARG
+
+
+def varlen(**kw):
+    a = dict(q=16, k=32, v=48, o=64, cu=80, batch=4, hq=16, hkv=16, max_s=16, d=128, scale=0.0)
+    a.update(kw)
+    return fmha_b200.load().fmha_forward_varlen(a["q"], a["k"], a["v"], a["o"], a["cu"], a["batch"],
+                                                a["hq"], a["hkv"], a["max_s"], a["d"], a["scale"],
+                                                None)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(cu=None), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(cu=82), _lib.FMHA_ERR_MISALIGNED),
+    (dict(scale=-1.0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(scale=float("nan")), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(max_s=17), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(max_s=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(d=64), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(q=8), _lib.FMHA_ERR_MISALIGNED),
+])
+def test_varlen_rejected_before_any_cuda_call(kw, status):
+    assert varlen(**kw) == status
+
+
+def test_varlen_empty_batch_is_a_noop():
+    assert varlen(batch=0, q=None, k=None, v=None, o=None, cu=None) == _lib.FMHA_OK
+
+
+def test_seqlens_poisson_matches_reference_generator(oracle):
+    """fmha_seqlens_poisson reproduces FMHAConfig::generate_seqlens_kv
+    (fmha_host.cpp:58-72) -- the reference build's own output."""
+    got = fmha_b200.seqlens_poisson(30720, 16)
+    assert got.min() >= 2 and got.max() <= 16 and abs(got.mean() - 4.4) < 0.2
+    if not oracle.ref_available():
+        pytest.skip("reference build absent")
+    assert np.array_equal(got, oracle.ref_generate_seqlens(30720, 16))
+    assert np.array_equal(fmha_b200.seqlens_poisson(100, 8), oracle.ref_generate_seqlens(100, 8))

@@ -1,0 +1,159 @@
+"""fmha_forward_varlen (the reference's packed K/V layout [sum S_b, Hkv, D] +
+cu_seqlens_kv, fmha_host.cpp:143-157) against the oracle's packed-layout
+restatement, the reference's own golden output and its Poisson(4) seqlens
+(fmha_host.cpp:58-72)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import fmha_b200
+from tests.test_parity_gpu import GUARD, POISON, check_close, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def seqlens(oracle, b, kind, rng):
+    if kind == "poisson":
+        if oracle.ref_available():
+            return oracle.ref_generate_seqlens(b, 16)
+        x = rng.poisson(4, size=4 * b + 64)
+        return x[(x >= 2) & (x <= 16)][:b].astype(np.int32)
+    if kind == "edge":
+        return np.array([(0, 1, 16, 2, 15, 3, 8, 9, 4, 5, 7, 6, 10, 11, 12, 13, 14)[i % 17]
+                         for i in range(b)], dtype=np.int32)
+    return np.full(b, int(kind), dtype=np.int32)
+
+
+def run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, max_s=16, scale=0.0):
+    cu = np.concatenate([[0], np.cumsum(sl)]).astype(np.int32)
+    n = b * hq * d
+    Q, K, V = to_dev(cuda, q), to_dev(cuda, k), to_dev(cuda, v)
+    CU = cuda.from_numpy(cu).cuda()
+    buf = cuda.full((n + 2 * GUARD,), POISON, dtype=cuda.int16, device="cuda")
+    O = buf[GUARD:GUARD + n]
+    lib = fmha_b200.load()
+    st = lib.fmha_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                 CU.data_ptr(), b, hq, hkv, max_s, d, scale, None)
+    assert st == 0, fmha_b200.status_string(st)
+    cuda.cuda.synchronize()
+    err = fmha_b200.device_error()
+    out = buf.cpu().numpy().view(np.uint16)
+    assert np.all(out[:GUARD] == POISON) and np.all(out[GUARD + n:] == POISON)
+    return out[GUARD:GUARD + n].copy(), err, cu
+
+
+CASES = [(b, hq, hkv, d, kind) for d in (128, 256) for (b, hq, hkv) in ((37, 16, 16), (20, 32, 32),
+                                                                       (9, 32, 16), (6, 8, 1))
+         for kind in ("poisson", "edge", "1", "3", "16")]
+
+
+@pytest.mark.parametrize("b,hq,hkv,d,kind", CASES, ids=str)
+def test_varlen_vs_oracle(cuda, oracle, b, hq, hkv, d, kind):
+    rng = np.random.default_rng(b * 7 + d)
+    sl = seqlens(oracle, b, kind, rng)
+    t = int(sl.sum())
+    q = oracle.gen_bf16(b * hq * d, 31, 1)
+    k = oracle.gen_bf16(t * hkv * d, 31, 2)
+    v = oracle.gen_bf16(t * hkv * d, 31, 3)
+    out, err, cu = run_varlen(cuda, q, k, v, sl, b, hq, hkv, d)
+    assert err == 0
+    ref32, _ = oracle.decode_thd(q, k, v, cu, b, hq, hkv, d)
+    check_close(out, ref32)
+
+
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "thd_*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=os.path.basename)
+def test_varlen_vs_reference_golden(cuda, oracle, path):
+    """The reference's own output on its own layout and seqlens, under its
+    own tolerance (fmha_host.cpp:260)."""
+    f = np.load(path)
+    b, h, d, seed = (int(f[x]) for x in ("batch", "heads", "head_dim", "seed"))
+    sl = f["seqlens"].astype(np.int32)
+    t = int(sl.sum())
+    q = oracle.gen_bf16(b * h * d, seed, 1)
+    k = oracle.gen_bf16(t * h * d, seed, 2)
+    v = oracle.gen_bf16(t * h * d, seed, 3)
+    out, err, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d)
+    assert err == 0
+    o = out.view(np.float16).astype(np.float32)
+    r = f["ref_o"].view(np.float16).astype(np.float32)
+    assert np.all(np.abs(o - r) <= 1e-2 + 1e-2 * np.abs(r))
+
+
+def test_varlen_uniform_matches_dense(cuda, oracle):
+    b, h, s, d = 64, 16, 5, 256
+    q, k, v = oracle.make_inputs_bhsd(b, h, h, s, d, seed=8)
+    packed = lambda x: np.ascontiguousarray(x.reshape(b, h, s, d).transpose(0, 2, 1, 3)).reshape(-1)  # noqa
+    out, err, _ = run_varlen(cuda, q, packed(k), packed(v), np.full(b, s, np.int32), b, h, h, d)
+    assert err == 0
+    from tests.test_parity_gpu import run_kernel
+    dense = run_kernel(cuda, q, k, v, b, h, h, s, d)
+    a = out.view(np.float16).astype(np.float32)
+    c = dense.view(np.float16).astype(np.float32)
+    assert np.abs(a - c).max() <= 2e-3
+
+
+def test_varlen_explicit_scale(cuda, oracle):
+    b, h, d = 5, 16, 128
+    sl = np.array([4, 4, 4, 4, 4], np.int32)
+    q = oracle.gen_bf16(b * h * d, 3, 1)
+    k = oracle.gen_bf16(20 * h * d, 3, 2)
+    v = oracle.gen_bf16(20 * h * d, 3, 3)
+    a, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=0.0)
+    c, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=1.0 / np.sqrt(d))
+    assert np.array_equal(a, c)
+    e, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=0.5)
+    assert not np.array_equal(a, e)
+
+
+def test_varlen_rejects_long_row_on_device(cuda, oracle):
+    """A row longer than max_seqlen_kv is skipped and flagged in the device
+    error word; the other rows are still computed."""
+    b, h, d = 4, 16, 128
+    sl = np.array([3, 9, 2, 5], np.int32)
+    t = int(sl.sum())
+    q = oracle.gen_bf16(b * h * d, 4, 1)
+    k = oracle.gen_bf16(t * h * d, 4, 2)
+    v = oracle.gen_bf16(t * h * d, 4, 3)
+    out, err, cu = run_varlen(cuda, q, k, v, sl, b, h, h, d, max_s=8)
+    assert err & 0xff == fmha_b200.FMHA_ERR_INVALID_ARG and (err >> 8) == 5
+    ref32, _ = oracle.decode_thd(q, k, v, cu, b, h, h, d)
+    n = h * d
+    for r in (0, 2, 3):
+        check_close(out[r * n:(r + 1) * n], ref32[r * n:(r + 1) * n])
+    assert np.all(out[n:2 * n] == POISON)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("hq,d", [(16, 128), (32, 256)])
+def test_varlen_full_size_reference_seqlens(cuda, oracle, hq, d):
+    """batch 30720 with the reference's own Poisson seqlens: sampled rows vs
+    the oracle, generated on the device."""
+    B = 30720
+    sl = seqlens(oracle, B, "poisson", np.random.default_rng(0))
+    cu = np.concatenate([[0], np.cumsum(sl)]).astype(np.int32)
+    t = int(cu[-1])
+    Q = cuda.empty(B * hq * d, dtype=cuda.bfloat16, device="cuda")
+    K = cuda.empty(t * hq * d, dtype=cuda.bfloat16, device="cuda")
+    V = cuda.empty_like(K)
+    for x, tid in ((Q, 1), (K, 2), (V, 3)):
+        fmha_b200.fill_normal_bf16(x, seed=0, tensor_id=tid)
+    O = cuda.empty(B * hq * d, dtype=cuda.float16, device="cuda")
+    CU = cuda.from_numpy(cu).cuda()
+    lib = fmha_b200.load()
+    assert lib.fmha_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                   CU.data_ptr(), B, hq, hq, 16, d, 0.0, None) == 0
+    cuda.cuda.synchronize()
+    assert fmha_b200.device_error() == 0
+    for b0 in (0, 1, 12345, B - 1):
+        s = int(sl[b0])
+        q = oracle.gen_bf16(hq * d, 0, 1, b0 * hq * d)
+        k = oracle.gen_bf16(s * hq * d, 0, 2, int(cu[b0]) * hq * d)
+        v = oracle.gen_bf16(s * hq * d, 0, 3, int(cu[b0]) * hq * d)
+        ref32, _ = oracle.decode_thd(q, k, v, np.array([0, s], np.int32), 1, hq, hq, d)
+        got = O[b0 * hq * d:(b0 + 1) * hq * d].cpu().view(cuda.int16).numpy().view(np.uint16)
+        check_close(got, ref32)
