@@ -276,6 +276,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-clocks", action="store_true",
                     help="skip the nvidia-smi sampler (profiling runs)")
+    ap.add_argument("--varlen-uniform", type=int, default=0,
+                    help="varlen configs: every row this long instead of Poisson(4) (profiling)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (small profiling cases only)")
     ap.add_argument("--sweep", action="store_true",
@@ -322,16 +324,19 @@ def main():
         names = [x for x in args.sweep_configs.split(",") if x] or sorted(CONFIGS)
         trials = [("ldg", None)] + [("bulk", int(w)) for w in args.sweep_warps.split(",") if w]
         for name in names:
+            cfg_n = CONFIGS[name]
+            if args.batch > 0:
+                cfg_n = (args.batch,) + tuple(cfg_n[1:])
             for var, warps in trials:
                 if warps is not None:
                     os.environ["FMHA_BULK_WARPS"] = str(warps)
                 if name in VARLEN:
                     if var != "ldg":
                         continue  # one varlen family
-                    r = time_varlen(torch, fmha_b200, CONFIGS[name], world, rank, args, barrier,
+                    r = time_varlen(torch, fmha_b200, cfg_n, world, rank, args, barrier,
                                     max_over_ranks, dev)
                 else:
-                    r = time_config(torch, fmha_b200, CONFIGS[name], world, rank, args, var,
+                    r = time_config(torch, fmha_b200, cfg_n, world, rank, args, var,
                                     barrier, max_over_ranks, dev, clocks=False)
                 if rank == 0:
                     print(json.dumps({"sweep": name, "variant": var, "warps": warps, **r}),
@@ -460,6 +465,8 @@ def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_rank
     import numpy as np
     b_all, hq, hkv, max_s, d = cfg
     sl_all = fmha_b200.seqlens_poisson(b_all, max_s, 42, 4.0)
+    if args.varlen_uniform > 0:
+        sl_all[:] = args.varlen_uniform
     lo, hi = shard(b_all, world, rank)
     b = hi - lo
     cu_all = np.concatenate([[0], np.cumsum(sl_all)]).astype(np.int64)

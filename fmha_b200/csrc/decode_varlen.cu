@@ -6,12 +6,11 @@
 // Work: batch row b has S_b = cu[b+1] - cu[b] rows per kv head; it is cut into
 // 16-row tiles of NU = 16/SMAX_b kv heads each (SMAX_b = next power of two
 // >= S_b), so short rows pack several heads into one tile and the score
-// reduction/softmax are paid once per 16 rows, as in the dense kernels. Tiles
-// are enumerated as t = b*TPB + j with TPB the tile count of a row of length
-// max_seqlen_kv; tiles past a row's own count are skipped. Persistent warps
-// take tiles round-robin, prefetch every K/V/Q row of the tile into registers
-// with 16-byte streaming loads, then run the shared tile math for the row's
-// SMAX_b (a warp-uniform switch over the five instantiations).
+// reduction/softmax are paid once per 16 rows, as in the dense kernels.
+// Persistent warps take batch rows round-robin and walk the row's tiles; for
+// each they prefetch every K/V/Q row into registers with 16-byte streaming
+// loads, then run the shared tile math for the row's SMAX_b (a warp-uniform
+// switch over the five instantiations).
 //
 // A row length outside [0, max_seqlen_kv] sets the device error word
 // (FMHA_ERR_INVALID_ARG, site 5) and that row's output is left unwritten; a
@@ -82,28 +81,37 @@ __global__ void __launch_bounds__(kLdgThreads) decode_varlen_kernel(const Varlen
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   float* sc = sc_all[warp];
-  const int64_t total = (int64_t)P.batch * P.tiles_per_row;
+  // Warps take whole batch rows round-robin and walk only the row's real
+  // tiles; the next row's cu_seqlens pair is loaded while this row runs.
   const int64_t stride = (int64_t)gridDim.x * WPB;
-  for (int64_t t = (int64_t)blockIdx.x * WPB + warp; t < total; t += stride) {
-    const int64_t b = t / P.tiles_per_row;
-    const int j = (int)(t - b * P.tiles_per_row);
-    const int c0 = __ldg(P.cu_seqlens + b);
-    const int s_len = __ldg(P.cu_seqlens + b + 1) - c0;
+  int64_t b = (int64_t)blockIdx.x * WPB + warp;
+  int c0n = 0, c1n = 0;
+  if (b < P.batch) {
+    c0n = __ldg(P.cu_seqlens + b);
+    c1n = __ldg(P.cu_seqlens + b + 1);
+  }
+  for (; b < P.batch; b += stride) {
+    const int c0 = c0n;
+    const int s_len = c1n - c0;
+    if (b + stride < P.batch) {
+      c0n = __ldg(P.cu_seqlens + b + stride);
+      c1n = __ldg(P.cu_seqlens + b + stride + 1);
+    }
     if (s_len < 0 || s_len > P.max_seqlen) {
-      if (j == 0 && lane == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
+      if (lane == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
       continue;
     }
     const int smax = s_len <= 1 ? 1 : s_len <= 2 ? 2 : s_len <= 4 ? 4 : s_len <= 8 ? 8 : 16;
     const int nu = 16 / smax;
-    if ((int64_t)j * nu >= P.num_heads_kv) continue;  // tile past this row's heads
-    const int h0 = j * nu;
-    const int nv = P.num_heads_kv - h0 < nu ? P.num_heads_kv - h0 : nu;
-    switch (smax) {
-      case 1: varlen_tile<D, 1, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
-      case 2: varlen_tile<D, 2, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
-      case 4: varlen_tile<D, 4, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
-      case 8: varlen_tile<D, 8, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
-      default: varlen_tile<D, 16, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
+    for (int h0 = 0; h0 < P.num_heads_kv; h0 += nu) {
+      const int nv = P.num_heads_kv - h0 < nu ? P.num_heads_kv - h0 : nu;
+      switch (smax) {
+        case 1: varlen_tile<D, 1, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
+        case 2: varlen_tile<D, 2, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
+        case 4: varlen_tile<D, 4, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
+        case 8: varlen_tile<D, 8, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
+        default: varlen_tile<D, 16, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
+      }
     }
   }
 }

@@ -364,14 +364,63 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
   const double scale = softmax_scale > 0.0f ? (double)softmax_scale
                                             : 1.0 / std::sqrt((double)head_dim);
   P.scale_log2 = (float)(1.4426950408889634 * scale);
-  int bps = 1;
-  st = blocks_per_sm(reinterpret_cast<KernelFn>(fn), kLdgThreads, &bps);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  // FMHA_VARLEN_KERNEL=ldg selects the register-prefetch kernel; the default
+  // is the gather ring.
+  static const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
+  if (kind && std::strcmp(kind, "ldg") == 0) {
+    int bps = 1;
+    st = blocks_per_sm(reinterpret_cast<KernelFn>(fn), kLdgThreads, &bps);
+    if (st != FMHA_OK) return st;
+    int64_t grid = (int64_t)dev.sms * bps;
+    const int64_t need = ((int64_t)batch + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
+    if (grid > need) grid = need;
+    fn<<<(unsigned)grid, kLdgThreads, 0, cs>>>(P);
+    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+  }
+  VarlenFn rfn = head_dim == 128 ? varlen_ring_kernel_d128(g) : varlen_ring_kernel_d256(g);
+  if (!rfn) return FMHA_ERR_UNSUPPORTED;
+  P.wait_timeout_ns = kWaitTimeoutNs;
+  int npw = env_int("FMHA_VARLEN_PRODUCERS", kVarlenProducers);  // measured best: 6
+  if (npw < 1) npw = 1;
+  if (npw > 8) npw = 8;
+  P.producers = npw;
+  int ncw = env_int("FMHA_VARLEN_WARPS", 8);
+  if (ncw < 1) ncw = 1;
+  if (ncw > kBulkMaxThreads / 32 - npw) ncw = kBulkMaxThreads / 32 - npw;
+  const uint32_t stage =
+      (kVarlenDescBytes + 32u * head_dim * 2 + 16u * g * head_dim * 2 + 127u) & ~127u;
+  P.sc_off = kHdrBytes;
+  P.ring_off = (P.sc_off + (uint32_t)ncw * g * 16 * 4 + 1023u) & ~1023u;
+  int ns = (int)((dev.smem_optin - (int64_t)P.ring_off) / stage);
+  const int ns_cap = env_int("FMHA_STAGES", kMaxStages);
+  if (ns > ns_cap) ns = ns_cap;
+  if (ns > kMaxStages) ns = kMaxStages;
+  // Producer and consumer warps both own whole stages: the stage count is a
+  // multiple of both warp counts, so stage st's phases are armed by one
+  // producer and consumed by one consumer, each in order, and no parity wait
+  // can refer to a phase two behind (try_wait.parity would call that one
+  // complete).
+  auto lcm = [](int a, int b) {
+    int x = a, y = b;
+    while (y) { const int t = x % y; x = y; y = t; }
+    return a / x * b;
+  };
+  while (lcm(npw, ncw) > ns && (ncw > 1 || npw > 1)) {
+    if (ncw > 1) --ncw;
+    else --npw;
+  }
+  P.producers = npw;
+  const int unit = lcm(npw, ncw);
+  if (unit > ns) return FMHA_ERR_UNSUPPORTED;
+  ns -= ns % unit;
+  P.stages = ns;
+  P.stage_bytes = stage;
+  const uint32_t smem = P.ring_off + (uint32_t)ns * stage;
+  st = ensure_smem(reinterpret_cast<KernelFn>(rfn), dev.smem_optin);
   if (st != FMHA_OK) return st;
-  const int64_t tiles = (int64_t)batch * P.tiles_per_row;
-  int64_t grid = (int64_t)dev.sms * bps;
-  const int64_t need = (tiles + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
-  if (grid > need) grid = need;
-  fn<<<(unsigned)grid, kLdgThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+  const int grid = batch < dev.sms ? batch : dev.sms;
+  rfn<<<grid, 32 * (npw + ncw), smem, cs>>>(P);
   return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
 }
 
