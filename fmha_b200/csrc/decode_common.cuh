@@ -545,12 +545,17 @@ struct VarlenParams {
   uint32_t sc_off;       // per-consumer-warp score scratch
   uint32_t ring_off;     // first stage
   int producers;         // gathering warps (ring kernel)
+  uint32_t chunk_max;    // chunk kernel: byte limit of one chunk (<= ring/2)
 };
 using VarlenFn = void (*)(const VarlenParams);
 VarlenFn varlen_kernel_d128(int g);
 VarlenFn varlen_kernel_d256(int g);
 VarlenFn varlen_ring_kernel_d128(int g);
 VarlenFn varlen_ring_kernel_d256(int g);
+VarlenFn varlen_chunk_kernel_d128(int g);
+VarlenFn varlen_chunk_kernel_d256(int g);
+constexpr int kVarlenSlots = 32;           // chunk descriptors in flight per CTA
+constexpr uint32_t kVarlenChunkHdr = 4096;  // barriers, counters, descriptors
 constexpr uint32_t kVarlenDescBytes = 64;
 constexpr int kVarlenProducers = 6;  // default gathering warps per varlen ring CTA
 

@@ -1,0 +1,308 @@
+// decode_varlen_chunk.cu -- packed-varlen decode attention streamed as whole
+// batch rows through a shared-memory byte ring (large 1-D bulk copies).
+//
+// Layout: K/V [sum_b S_b, Hkv, D] with cu_seqlens_kv[B+1]
+// (fmha_host.cpp:143-157), Q/O [B, Hq, 1, D].
+//
+// In the packed layout the K rows of one batch row b, all kv heads, are one
+// contiguous block of S_b*Hkv*D elements (so are its V rows, and its Hq query
+// rows). A *chunk* is that block -- or, when a row is too long for the chunk
+// limit, the rows of a group of nh consecutive kv heads, whose K rows at one
+// position s are one contiguous run of nh*D elements.
+//
+// Per CTA (persistent, one per SM): a contiguous range of batch rows.
+//  * Producer (warp 0) walks the rows in order (cu_seqlens read 31 rows per
+//    warp load), allocates each chunk in a circular byte ring (a chunk never
+//    wraps: the tail skips to the ring start instead), writes the chunk's
+//    descriptor into slot c % kSlots, arms the slot's `full` mbarrier with the
+//    chunk's byte count and issues the copies: one bulk copy each for K, V and
+//    Q of a whole row, or one K and one V copy per position for a head group.
+//    It then publishes the chunk count. Ring space and slots are reclaimed in
+//    chunk order by waiting on each slot's `empty` mbarrier, one phase after
+//    another (a single producer walks every slot's phases in order).
+//  * Consumers (all other warps) take 16-row tiles (NU = 16/SMAX_b kv heads of
+//    one chunk) from a shared atomic tile counter, find the tile's chunk among
+//    the published ones, wait for its `full` phase (published => armed, so the
+//    parity names the right phase), run the shared tile math from shared
+//    memory and stream fp16 rows to O. The last tile of a chunk resets the
+//    chunk's tile counter and arrives on its `empty` mbarrier.
+//
+// A row length outside [0, max_seqlen_kv] sets the device error word
+// (FMHA_ERR_INVALID_ARG, site 5) and the row is skipped; a zero-length row
+// yields zeros. Every wait is bounded (globaltimer) and never traps; on exit
+// the producer waits (bounded) for its own copies still in flight.
+//
+// Compiled once per head_dim: -DFMHA_HEAD_DIM=128 or 256.
+#include "decode_common.cuh"
+
+#ifndef FMHA_HEAD_DIM
+#error "compile with -DFMHA_HEAD_DIM=128 or 256"
+#endif
+
+namespace fmha {
+
+namespace {
+
+struct ChunkDesc {
+  int64_t b;          // batch row
+  int64_t end_total;  // ring bytes allocated up to the end of this chunk
+  uint32_t off;       // chunk start in the ring
+  uint32_t kv_bytes;  // bytes of the K block (= of the V block)
+  int s_len;          // rows per head
+  int smax;           // power of two >= s_len
+  int h0;             // first kv head of the chunk
+  int nh;             // kv heads in the chunk
+  int tile_base;      // CTA-local index of the chunk's first tile
+  int ntiles;
+};
+static_assert(sizeof(ChunkDesc) == 48, "descriptor size");
+
+__device__ __forceinline__ int smax_of(int s) {
+  return s <= 1 ? 1 : s <= 2 ? 2 : s <= 4 ? 4 : s <= 8 ? 8 : 16;
+}
+
+template <int D, int SMAX, int G>
+__device__ __forceinline__ void chunk_tile(const VarlenParams& P, const ChunkDesc& c, int hl0,
+                                           uint32_t cbase, float* sc, int lane) {
+  using T = Tile16<D, SMAX, G>;
+  const int r0 = lane / T::LPR;
+  const int cl = lane % T::LPR;
+  const int nh = c.nh;
+  const int nv = nh - hl0 < T::NU ? nh - hl0 : T::NU;
+  const uint32_t kl = cbase + cl * 16;
+  const uint32_t vl = kl + c.kv_bytes;
+  const uint32_t ql = cbase + 2 * c.kv_bytes + cl * 16;
+  // Tile row r = (unit u, position s) is chunk row s*nh + hl0 + u.
+  auto rowoff = [&](int p) -> uint32_t {
+    const int r = r0 * T::NP + p;
+    return (uint32_t)((r % SMAX) * nh + hl0 + r / SMAX) * (D * 2);
+  };
+  auto loadK = [&](int p) { return lds128(kl + rowoff(p)); };
+  auto loadV = [&](int p) { return lds128(vl + rowoff(p)); };
+  auto loadQ = [&](int, int u, int g) {
+    return lds128(ql + (uint32_t)((hl0 + u) * G + g) * (D * 2));
+  };
+  const int64_t qrow0 = (c.b * P.num_heads_kv + c.h0 + hl0) * G;
+  auto store = [&](int u, const float (&acc)[G][8]) {
+    if (u >= nv) return;
+    uint16_t* orow = P.O + (qrow0 + u * G) * D + cl * 8;
+#pragma unroll
+    for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
+  };
+  attend_tile16<D, SMAX, G>(loadK, loadV, loadQ, store, c.s_len, nv, P.scale_log2, sc, lane);
+}
+
+}  // namespace
+
+template <int D, int G>
+__global__ void __launch_bounds__(kBulkMaxThreads, 1)
+    decode_varlen_chunk_kernel(const VarlenParams P) {
+  constexpr int M = kVarlenSlots;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(smem);
+  const uint32_t empty0 = full0 + 8u * M;
+  volatile int* ctrl = reinterpret_cast<volatile int*>(smem + 16 * M);
+  volatile int* abort_flag = ctrl + 0;
+  volatile int* published = ctrl + 1;    // chunks whose copies are armed
+  volatile int* total_tiles = ctrl + 2;  // tile count once the producer is done, else -1
+  int* next_tile = const_cast<int*>(ctrl + 3);
+  int* done = const_cast<int*>(ctrl + 4);  // [M] tiles finished per slot
+  ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(smem + 16 * M + 4 * (4 + M));
+  unsigned char* ring = smem + P.ring_off;
+  const uint32_t ring0 = smem_u32(ring);
+  const uint32_t R = P.stage_bytes;  // ring size in bytes (multiple of 128)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < M; ++i) {
+      mbar_init(full0 + 8u * i, 1);
+      mbar_init(empty0 + 8u * i, 1);
+      done[i] = 0;
+    }
+    *abort_flag = 0;
+    *published = 0;
+    *total_tiles = -1;
+    *next_tile = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  const int64_t row_lo = P.batch * blockIdx.x / gridDim.x;
+  const int64_t row_hi = P.batch * (blockIdx.x + 1) / gridDim.x;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const int hkv = P.num_heads_kv;
+    const uint64_t policy = policy_evict_first();
+    int64_t tail = 0, head = 0;  // ring bytes ever allocated / ever released
+    int c = 0, oldest = 0, tiles = 0;
+    bool stop = false;
+    for (int64_t base = row_lo; base < row_hi && !stop; base += 31) {
+      const int64_t idx = base + lane;
+      const int cu_l = idx <= row_hi ? __ldg(P.cu_seqlens + idx) : 0;
+      const int nrows = row_hi - base < 31 ? (int)(row_hi - base) : 31;
+      for (int i = 0; i < nrows && !stop; ++i) {
+        const int c0 = __shfl_sync(kFullMask, cu_l, i);
+        const int s_len = __shfl_sync(kFullMask, cu_l, i + 1) - c0;
+        const int64_t b = base + i;
+        if (s_len < 0 || s_len > P.max_seqlen) {
+          if (lane == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
+          continue;
+        }
+        const int smax = smax_of(s_len);
+        const int nu = 16 / smax;
+        const uint32_t per_head = (uint32_t)(2 * s_len + G) * (D * 2);
+        int nh_max = (int)(P.chunk_max / per_head);
+        if (nh_max < 1) nh_max = 1;
+        if (nh_max > hkv) nh_max = hkv;
+        if (nh_max < hkv && nh_max >= nu) nh_max -= nh_max % nu;  // whole tiles per group
+        for (int h0 = 0; h0 < hkv && !stop; h0 += nh_max) {
+          const int nh = hkv - h0 < nh_max ? hkv - h0 : nh_max;
+          const uint32_t kvb = (uint32_t)s_len * nh * (D * 2);
+          const uint32_t qb = (uint32_t)(nh * G) * (D * 2);
+          const uint32_t sz = (2 * kvb + qb + 127u) & ~127u;
+          const uint32_t pos = (uint32_t)(tail % R);
+          const uint32_t pad = pos + sz > R ? R - pos : 0u;
+          // Reclaim chunks in order until the slot is free and the bytes fit.
+          while (oldest <= c - M || tail + pad + sz - head > (int64_t)R) {
+            if (!mbar_wait(empty0 + 8u * (oldest % M), (oldest / M) & 1, abort_flag, P.err,
+                           P.wait_timeout_ns, kSiteProducerEmpty)) {
+              stop = true;
+              break;
+            }
+            head = desc[oldest % M].end_total;
+            ++oldest;
+          }
+          if (stop) break;
+          const int64_t start = tail + pad;
+          const uint32_t off = (uint32_t)(start % R);
+          tail = start + sz;
+          const int nt = (nh + nu - 1) / nu;
+          const int slot = c % M;
+          const uint32_t bar = full0 + 8u * slot;
+          if (lane == 0) {
+            ChunkDesc& d = desc[slot];
+            d.b = b;
+            d.end_total = tail;
+            d.off = off;
+            d.kv_bytes = kvb;
+            d.s_len = s_len;
+            d.smax = smax;
+            d.h0 = h0;
+            d.nh = nh;
+            d.tile_base = tiles;
+            d.ntiles = nt;
+            mbar_arrive_expect_tx(bar, 2 * kvb + qb);
+          }
+          __syncwarp();
+          const uint32_t dst = ring0 + off;
+          const int64_t qsrc = (b * hkv + h0) * G * D;
+          if (nh == hkv) {
+            const int64_t ksrc = (int64_t)c0 * hkv * D;
+            if (lane == 0 && kvb) bulk_g2s(dst, P.K + ksrc, kvb, bar, policy);
+            if (lane == 1 && kvb) bulk_g2s(dst + kvb, P.V + ksrc, kvb, bar, policy);
+            if (lane == 2) bulk_g2s(dst + 2 * kvb, P.Q + qsrc, qb, bar, policy);
+          } else {
+            const uint32_t run = (uint32_t)nh * (D * 2);
+            if (lane < s_len) {
+              const int64_t ksrc = ((int64_t)(c0 + lane) * hkv + h0) * D;
+              bulk_g2s(dst + lane * run, P.K + ksrc, run, bar, policy);
+              bulk_g2s(dst + kvb + lane * run, P.V + ksrc, run, bar, policy);
+            }
+            if (lane == 31) bulk_g2s(dst + 2 * kvb, P.Q + qsrc, qb, bar, policy);
+          }
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence_block();
+            *published = c + 1;
+          }
+          tiles += nt;
+          ++c;
+        }
+      }
+    }
+    if (lane == 0) {
+      __threadfence_block();
+      if (!stop) *total_tiles = tiles;
+      else *abort_flag = 1;
+      // Never leave the CTA with copies in flight into its shared memory.
+      for (int j = oldest; j < c; ++j)
+        mbar_wait(full0 + 8u * (j % M), (j / M) & 1, nullptr, P.err, P.wait_timeout_ns,
+                  kSiteDrain);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  float* sc = reinterpret_cast<float*>(smem + P.sc_off) + cw * (G * 16);
+  for (;;) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(next_tile, 1);
+    t = __shfl_sync(kFullMask, t, 0);
+    // Wait (bounded) until a published chunk holds tile t, or there is none.
+    int c = -1;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      const int pub = *published;
+      __threadfence_block();  // descriptors of chunks < pub are visible
+      if (pub > 0) {
+        const ChunkDesc& last = desc[(pub - 1) % M];
+        if (t < last.tile_base + last.ntiles) {
+          c = pub - 1;
+          while (desc[c % M].tile_base > t) --c;  // within the last M chunks
+          break;
+        }
+      }
+      const int tot = *total_tiles;
+      if ((tot >= 0 && t >= tot) || *abort_flag) break;
+      if ((it & 15u) == 15u && globaltimer_ns() - t0 > P.wait_timeout_ns) {
+        report_device_error(P.err, 5u /* FMHA_ERR_DEVICE_TIMEOUT */, kSiteConsumerIssued);
+        *abort_flag = 1;
+        break;
+      }
+    }
+    if (c < 0) break;
+    const int slot = c % M;
+    if (!mbar_wait(full0 + 8u * slot, (c / M) & 1, abort_flag, P.err, P.wait_timeout_ns,
+                   kSiteConsumerFull))
+      break;
+    const ChunkDesc d = desc[slot];
+    const int nu = 16 / d.smax;
+    const int hl0 = (t - d.tile_base) * nu;
+    const uint32_t cbase = ring0 + d.off;
+    switch (d.smax) {
+      case 1: chunk_tile<D, 1, G>(P, d, hl0, cbase, sc, lane); break;
+      case 2: chunk_tile<D, 2, G>(P, d, hl0, cbase, sc, lane); break;
+      case 4: chunk_tile<D, 4, G>(P, d, hl0, cbase, sc, lane); break;
+      case 8: chunk_tile<D, 8, G>(P, d, hl0, cbase, sc, lane); break;
+      default: chunk_tile<D, 16, G>(P, d, hl0, cbase, sc, lane); break;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      // The chunk's last tile resets the slot's counter and frees the chunk.
+      if (atomicAdd(done + slot, 1) == d.ntiles - 1) {
+        done[slot] = 0;
+        __threadfence_block();
+        mbar_arrive(empty0 + 8u * slot);
+      }
+    }
+  }
+}
+
+#define FMHA_CAT2(a, b) a##b
+#define FMHA_CAT(a, b) FMHA_CAT2(a, b)
+
+VarlenFn FMHA_CAT(varlen_chunk_kernel_d, FMHA_HEAD_DIM)(int g) {
+  constexpr int D = FMHA_HEAD_DIM;
+  switch (g) {
+    case 1: return decode_varlen_chunk_kernel<D, 1>;
+    case 2: return decode_varlen_chunk_kernel<D, 2>;
+    case 4: return decode_varlen_chunk_kernel<D, 4>;
+    case 8: return decode_varlen_chunk_kernel<D, 8>;
+    default: return nullptr;
+  }
+}
+
+}  // namespace fmha

@@ -365,8 +365,8 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
                                             : 1.0 / std::sqrt((double)head_dim);
   P.scale_log2 = (float)(1.4426950408889634 * scale);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  // FMHA_VARLEN_KERNEL=ldg selects the register-prefetch kernel; the default
-  // is the gather ring.
+  // FMHA_VARLEN_KERNEL=ldg selects the register-prefetch kernel, =ring the
+  // gather ring; the default is the chunk ring.
   static const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
   if (kind && std::strcmp(kind, "ldg") == 0) {
     int bps = 1;
@@ -376,6 +376,30 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
     const int64_t need = ((int64_t)batch + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
     if (grid > need) grid = need;
     fn<<<(unsigned)grid, kLdgThreads, 0, cs>>>(P);
+    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+  }
+  if (!(kind && std::strcmp(kind, "ring") == 0)) {
+    // Default: whole packed rows (or head groups) as chunks of a byte ring.
+    VarlenFn cfn = head_dim == 128 ? varlen_chunk_kernel_d128(g) : varlen_chunk_kernel_d256(g);
+    if (!cfn) return FMHA_ERR_UNSUPPORTED;
+    P.wait_timeout_ns = kWaitTimeoutNs;
+    int ncw = env_int("FMHA_VARLEN_WARPS", 16);
+    if (ncw < 1) ncw = 1;
+    if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
+    P.sc_off = kVarlenChunkHdr;
+    P.ring_off = (P.sc_off + (uint32_t)ncw * g * 16 * 4 + 1023u) & ~1023u;
+    const uint32_t ring = (uint32_t)(dev.smem_optin - (int64_t)P.ring_off) & ~127u;
+    P.stage_bytes = ring;
+    uint32_t cmax = (uint32_t)env_int("FMHA_VARLEN_CHUNK", 96 * 1024);
+    if (cmax > ring / 2) cmax = ring / 2;
+    // One head of the longest row must fit in a chunk.
+    const uint32_t one = (uint32_t)(2 * max_seqlen_kv + g) * head_dim * 2;
+    if (one > cmax) return FMHA_ERR_UNSUPPORTED;
+    P.chunk_max = cmax;
+    st = ensure_smem(reinterpret_cast<KernelFn>(cfn), dev.smem_optin);
+    if (st != FMHA_OK) return st;
+    const int grid = batch < dev.sms ? batch : dev.sms;
+    cfn<<<grid, 32 * (1 + ncw), P.ring_off + ring, cs>>>(P);
     return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
   }
   VarlenFn rfn = head_dim == 128 ? varlen_ring_kernel_d128(g) : varlen_ring_kernel_d256(g);
