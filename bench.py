@@ -221,6 +221,15 @@ def run_reference_arm(args, cfg_name, cfg):
 def config_block(name, cfg, n_gpus):
     b, hq, hkv, s, d = cfg
     total = algo_bytes(b, hq, hkv, s, d)
+    if name in VARLEN:
+        return {"workload": f"decode attention {name}: batch={b} seqlen_q=1 seqlen_kv "
+                            f"Poisson(4) in [2,{s}] (seed 42, the reference's table) "
+                            f"num_heads_q={hq} num_heads_kv={hkv} head_dim={d}",
+                "batch": b, "seqlen_q": 1, "max_seqlen_kv": s, "num_heads_q": hq,
+                "num_heads_kv": hkv, "head_dim": d,
+                "layout": "Q/O [B,H,1,D], K/V packed [sum S_b,Hkv,D] + cu_seqlens_kv",
+                "global_batch": b, "parallelism": f"batch-shard x{n_gpus} (no collective)",
+                "l2": "inputs larger than L2; no flush"}
     return {"workload": f"decode attention {name}: batch={b} seqlen_q=1 seqlen_kv={s} "
                         f"num_heads_q={hq} num_heads_kv={hkv} head_dim={d}",
             "batch": b, "seqlen_q": 1, "seqlen_kv": s, "num_heads_q": hq, "num_heads_kv": hkv,
@@ -347,8 +356,15 @@ def main():
     cfg = CONFIGS[args.config]
     if args.batch > 0:
         cfg = (args.batch,) + tuple(cfg[1:])
-    r = time_config(torch, fmha_b200, cfg, world, rank, args, args.variant, barrier,
-                    max_over_ranks, dev, clocks=not args.no_clocks)
+    varlen = args.config in VARLEN
+    if varlen:
+        # The reference's own table: packed K/V, Poisson(4) seqlens (device time
+        # only; the e2e and CPU legs are defined for the dense north-star call).
+        r = time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev)
+        args.no_e2e = args.no_cpu = True
+    else:
+        r = time_config(torch, fmha_b200, cfg, world, rank, args, args.variant, barrier,
+                        max_over_ranks, dev, clocks=not args.no_clocks)
     e2e = None
     if not args.no_e2e:
         e2e = e2e_leg(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev)
@@ -358,7 +374,7 @@ def main():
     if rank == 0:
         peak, peak_src = peak_hbm()
         b, hq, hkv, s, d = cfg
-        per_launch_bytes = algo_bytes(b // world, hq, hkv, s, d)
+        per_launch_bytes = (r["bytes_total"] if varlen else algo_bytes(b, hq, hkv, s, d)) / world
         achieved = per_launch_bytes / (r["kernel_ms"] * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": r["value"], "unit": "TB/s", "n_gpus": world,
@@ -508,7 +524,8 @@ def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_rank
     del Q, K, V, O
     torch.cuda.empty_cache()
     return {"value": round(total / (ms_max * 1e-3) / 1e12, 4), "ms_per_step": round(ms_max, 5),
-            "kernel_ms": ms, "clocks": None, "mean_seqlen": float(sl_all.mean())}
+            "kernel_ms": ms, "clocks": None, "mean_seqlen": float(sl_all.mean()),
+            "bytes_total": total}
 
 
 def local_gpu_index(dev, r):

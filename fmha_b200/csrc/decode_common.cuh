@@ -66,6 +66,10 @@ struct Params {
   uint32_t q_off;       // Q offset inside a stage
   uint32_t sc_off;      // per-warp score scratch offset in shared memory
   uint32_t ring_off;    // first stage offset in shared memory
+  // fused KV-cache append (ldg family, APPEND instantiations only)
+  const uint16_t* K_new;  // [units, D]: this step's K row of every unit
+  const uint16_t* V_new;
+  int64_t kv_ustride;     // elements between consecutive units' K slabs (cache stride)
 };
 
 template <int D, int SMAX, int G>
@@ -520,7 +524,7 @@ struct LdgTpi {
 // Kernel entry points (defined in decode_bulk.cu / decode_ldg.cu).
 template <int D, int SMAX, int G>
 __global__ void decode_bulk_kernel(const Params P);
-template <int D, int SMAX, int G, int TPI>
+template <int D, int SMAX, int G, int TPI, bool APPEND>
 __global__ void decode_ldg_kernel(const Params P);
 
 using KernelFn = void (*)(const Params);
@@ -564,5 +568,7 @@ KernelFn bulk_kernel_d128(int smax, int g);
 KernelFn bulk_kernel_d256(int smax, int g);
 KernelFn ldg_kernel_d128(int smax, int g);
 KernelFn ldg_kernel_d256(int smax, int g);
+KernelFn ldg_append_kernel_d128(int smax, int g);
+KernelFn ldg_append_kernel_d256(int smax, int g);
 
 }  // namespace fmha

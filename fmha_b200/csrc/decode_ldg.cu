@@ -17,7 +17,11 @@
 
 namespace fmha {
 
-template <int D, int SMAX, int G, int TPI>
+// APPEND: the K/V slabs are rows 0..s_len-1 of a cache with P.kv_ustride
+// elements per unit; row s_len-1 is this step's new row, read from
+// P.K_new/P.V_new ([units, D]) and also written into the cache, in the same
+// pass (fused KV-cache append + attend).
+template <int D, int SMAX, int G, int TPI, bool APPEND>
 __global__ void __launch_bounds__(kLdgThreads) decode_ldg_kernel(const Params P) {
   using T = TileShape<D, SMAX, G>;
   constexpr int WPB = kLdgThreads / 32;
@@ -41,15 +45,24 @@ __global__ void __launch_bounds__(kLdgThreads) decode_ldg_kernel(const Params P)
       const int64_t tile_u0 = (t0 + i) * T::NU;
       const int64_t left = P.units - tile_u0;
       uv[i] = left <= 0 ? 0 : (left < T::NU ? (int)left : T::NU);
-      const uint16_t* kb = P.K + tile_u0 * s_len * D + cl * 8;
-      const uint16_t* vb = P.V + tile_u0 * s_len * D + cl * 8;
+      const int64_t ustride = APPEND ? P.kv_ustride : (int64_t)s_len * D;
+      const uint16_t* kb = P.K + tile_u0 * ustride + cl * 8;
+      const uint16_t* vb = P.V + tile_u0 * ustride + cl * 8;
 #pragma unroll
       for (int p = 0; p < T::NP; ++p) {
         const int r = p * T::RPP + r0;
-        const int64_t off = (int64_t)((r / SMAX) * s_len + (r % SMAX)) * D;
+        const int64_t off = (int64_t)(r / SMAX) * ustride + (int64_t)(r % SMAX) * D;
         const bool ok = (r % SMAX) < s_len && (r / SMAX) < uv[i];
-        kr[i][p] = ok ? ldg_stream(kb + off) : make_uint4(0, 0, 0, 0);
-        vr[i][p] = ok ? ldg_stream(vb + off) : make_uint4(0, 0, 0, 0);
+        if (APPEND && ok && (r % SMAX) == s_len - 1) {
+          const int64_t noff = (tile_u0 + r / SMAX) * D + cl * 8;
+          kr[i][p] = ldg_stream(P.K_new + noff);
+          vr[i][p] = ldg_stream(P.V_new + noff);
+          stg_stream(const_cast<uint16_t*>(kb + off), kr[i][p]);
+          stg_stream(const_cast<uint16_t*>(vb + off), vr[i][p]);
+        } else {
+          kr[i][p] = ok ? ldg_stream(kb + off) : make_uint4(0, 0, 0, 0);
+          vr[i][p] = ok ? ldg_stream(vb + off) : make_uint4(0, 0, 0, 0);
+        }
       }
 #pragma unroll
       for (int g = 0; g < G; ++g)
@@ -80,7 +93,30 @@ __global__ void __launch_bounds__(kLdgThreads) decode_ldg_kernel(const Params P)
 
 KernelFn FMHA_CAT(ldg_kernel_d, FMHA_HEAD_DIM)(int smax, int g) {
   constexpr int D = FMHA_HEAD_DIM;
-#define FMHA_K(SM, GG) decode_ldg_kernel<D, SM, GG, LdgTpi<D, SM, GG>::value>
+#define FMHA_K(SM, GG) decode_ldg_kernel<D, SM, GG, LdgTpi<D, SM, GG>::value, false>
+#define FMHA_G(SM)                    \
+  switch (g) {                        \
+    case 1: return FMHA_K(SM, 1);     \
+    case 2: return FMHA_K(SM, 2);     \
+    case 4: return FMHA_K(SM, 4);     \
+    case 8: return FMHA_K(SM, 8);     \
+    default: return nullptr;          \
+  }
+  switch (smax) {
+    case 1: FMHA_G(1)
+    case 2: FMHA_G(2)
+    case 4: FMHA_G(4)
+    case 8: FMHA_G(8)
+    case 16: FMHA_G(16)
+    default: return nullptr;
+  }
+#undef FMHA_G
+#undef FMHA_K
+}
+
+KernelFn FMHA_CAT(ldg_append_kernel_d, FMHA_HEAD_DIM)(int smax, int g) {
+  constexpr int D = FMHA_HEAD_DIM;
+#define FMHA_K(SM, GG) decode_ldg_kernel<D, SM, GG, LdgTpi<D, SM, GG>::value, true>
 #define FMHA_G(SM)                    \
   switch (g) {                        \
     case 1: return FMHA_K(SM, 1);     \

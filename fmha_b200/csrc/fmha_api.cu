@@ -224,8 +224,10 @@ int ldg_tpi(int smax, int g) {
 }
 
 fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev,
-                         cudaStream_t stream) {
-  KernelFn fn = d == 128 ? ldg_kernel_d128(smax, g) : ldg_kernel_d256(smax, g);
+                         cudaStream_t stream, bool append = false) {
+  KernelFn fn = append ? (d == 128 ? ldg_append_kernel_d128(smax, g)
+                                   : ldg_append_kernel_d256(smax, g))
+                       : (d == 128 ? ldg_kernel_d128(smax, g) : ldg_kernel_d256(smax, g));
   if (!fn) return FMHA_ERR_UNSUPPORTED;
   const int rpp = rows_per_access(d);
   const int rows = smax > rpp ? smax : rpp;
@@ -446,6 +448,39 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
   const int grid = batch < dev.sms ? batch : dev.sms;
   rfn<<<grid, 32 * (npw + ncw), smem, cs>>>(P);
   return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+}
+
+fmha_status_t fmha_forward_append(const void* Q, void* K_cache, void* V_cache,
+                                  const void* K_new, const void* V_new, void* O, int batch,
+                                  int num_heads_q, int num_heads_kv, int seqlen_kv,
+                                  int cache_seqlen, int head_dim, fmha_stream_t stream) {
+  fmha_status_t st =
+      check_args(Q, K_cache, V_cache, O, batch, num_heads_q, num_heads_kv, seqlen_kv, head_dim);
+  if (st != FMHA_OK) return st;
+  if (batch > 0 && (!K_new || !V_new)) return FMHA_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(K_new) | reinterpret_cast<uintptr_t>(V_new)) & 15u)
+    return FMHA_ERR_MISALIGNED;
+  if (cache_seqlen < seqlen_kv) return FMHA_ERR_INVALID_ARG;
+  if (batch == 0) return FMHA_OK;
+  DeviceInfo dev;
+  st = device_info(&dev);
+  if (st != FMHA_OK) return st;
+  Params P;
+  std::memset(&P, 0, sizeof(P));
+  P.Q = static_cast<const uint16_t*>(Q);
+  P.K = static_cast<const uint16_t*>(K_cache);
+  P.V = static_cast<const uint16_t*>(V_cache);
+  P.O = static_cast<uint16_t*>(O);
+  P.K_new = static_cast<const uint16_t*>(K_new);
+  P.V_new = static_cast<const uint16_t*>(V_new);
+  P.kv_ustride = (int64_t)cache_seqlen * head_dim;
+  P.err = dev.err;
+  P.wait_timeout_ns = kWaitTimeoutNs;
+  P.units = (int64_t)batch * num_heads_kv;
+  P.s_len = seqlen_kv;
+  P.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+  return launch_ldg(P, head_dim, smax_for(seqlen_kv), num_heads_q / num_heads_kv, dev,
+                    reinterpret_cast<cudaStream_t>(stream), true);
 }
 
 fmha_status_t fmha_forward(const void* Q, const void* K, const void* V, void* O, int batch,

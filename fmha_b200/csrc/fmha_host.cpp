@@ -19,7 +19,11 @@
 //
 // Usage: fmha_host [config_index] [--all] [--gpus N] [--iters N] [--warmups N]
 //                  [--seqlen S] [--seed S] [--variant auto|bulk|ldg]
-//                  [--validate-rows N] [--json]
+//                  [--validate-rows N] [--json] [--varlen]
+//
+// --varlen runs the reference's own benchmark exactly: packed K/V
+// [sum S_b, Hkv, D] with cu_seqlens_kv and Poisson(4) lengths in [2, 16]
+// from mt19937(42) (fmha_host.cpp:58-82), through fmha_forward_varlen.
 #include <cuda_runtime.h>
 #include <omp.h>
 
@@ -87,6 +91,7 @@ struct Options {
   int variant = FMHA_VARIANT_AUTO;
   int validate_rows = 64;
   bool json = false;
+  bool varlen = false;  // the reference's packed layout and Poisson(4) seqlens
 };
 
 // ------------------------------------------------------------ host generator
@@ -139,18 +144,20 @@ void gen_bf16(uint16_t* out, int64_t n, uint64_t seed, uint32_t tensor, int64_t 
 // ------------------------------------------------------------ CPU check
 // One batch row, all heads: fp32 softmax(q.k^T/sqrt(D)) v in the reference's
 // operation order (fmha_host.cpp:179-243), P kept in fp32.
+// K/V element (head kvh, position j, column c) is at kvh*head_stride +
+// j*row_stride + c: [B,H,S,D] has (S*D, D), the packed layout (D, Hkv*D).
 void cpu_row(const uint16_t* q, const uint16_t* k, const uint16_t* v, int hq, int hkv, int s,
-             int d, float* out) {
+             int d, int64_t head_stride, int64_t row_stride, float* out) {
   const int g = hq / hkv;
   for (int h = 0; h < hq; ++h) {
     const int kvh = h / g;
     const uint16_t* qh = q + (int64_t)h * d;
-    const uint16_t* kh = k + (int64_t)kvh * s * d;
-    const uint16_t* vh = v + (int64_t)kvh * s * d;
+    const uint16_t* kh = k + (int64_t)kvh * head_stride;
+    const uint16_t* vh = v + (int64_t)kvh * head_stride;
     float sc[16];
     for (int j = 0; j < s; ++j) {
       float acc = 0.f;
-      for (int c = 0; c < d; ++c) acc += bf16_to_f32(qh[c]) * bf16_to_f32(kh[(int64_t)j * d + c]);
+      for (int c = 0; c < d; ++c) acc += bf16_to_f32(qh[c]) * bf16_to_f32(kh[(int64_t)j * row_stride + c]);
       sc[j] = acc * (1.0f / std::sqrt((float)d));
     }
     float mx = -INFINITY;
@@ -160,7 +167,7 @@ void cpu_row(const uint16_t* q, const uint16_t* k, const uint16_t* v, int hq, in
     for (int j = 0; j < s; ++j) sc[j] = std::exp(sc[j] - mx) / sum;
     for (int c = 0; c < d; ++c) {
       float acc = 0.f;
-      for (int j = 0; j < s; ++j) acc += sc[j] * bf16_to_f32(vh[(int64_t)j * d + c]);
+      for (int j = 0; j < s; ++j) acc += sc[j] * bf16_to_f32(vh[(int64_t)j * row_stride + c]);
       out[(int64_t)h * d + c] = acc;
     }
   }
@@ -194,12 +201,16 @@ struct ShardResult {
   int device_error = 0;
 };
 
+// cu: global cu_seqlens (varlen mode) or empty.
 void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64_t rows,
-               HostBarrier& bar, ShardResult& res) {
+               const std::vector<int64_t>& cu, HostBarrier& bar, ShardResult& res) {
   CUDA_CHECK(cudaSetDevice(gpu));
   const int hq = cfg.num_heads_q, hkv = cfg.num_heads_kv, d = cfg.head_dim, s = o.seqlen;
-  const int64_t nq = rows * hq * d, nkv = rows * hkv * s * d;
-  void *dQ, *dK, *dV, *dO;
+  const bool vl = o.varlen;
+  const int64_t t0row = vl ? cu[row0] : row0 * s;  // first K/V row (packed) of the shard
+  const int64_t nq = rows * hq * d;
+  const int64_t nkv = vl ? (cu[row0 + rows] - cu[row0]) * hkv * d : rows * hkv * s * d;
+  void *dQ, *dK, *dV, *dO, *dCu = nullptr;
   CUDA_CHECK(cudaMalloc(&dQ, nq * 2));
   CUDA_CHECK(cudaMalloc(&dK, nkv * 2));
   CUDA_CHECK(cudaMalloc(&dV, nkv * 2));
@@ -208,11 +219,22 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
   CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
   fmha_stream_t fs = reinterpret_cast<fmha_stream_t>(st);
   FMHA_CHECK(fmha_fill_normal_bf16(dQ, nq, o.seed, 1, row0 * hq * d, fs));
-  FMHA_CHECK(fmha_fill_normal_bf16(dK, nkv, o.seed, 2, row0 * hkv * s * d, fs));
-  FMHA_CHECK(fmha_fill_normal_bf16(dV, nkv, o.seed, 3, row0 * hkv * s * d, fs));
+  FMHA_CHECK(fmha_fill_normal_bf16(dK, nkv, o.seed, 2, t0row * hkv * d, fs));
+  FMHA_CHECK(fmha_fill_normal_bf16(dV, nkv, o.seed, 3, t0row * hkv * d, fs));
   CUDA_CHECK(cudaMemsetAsync(dO, 0, nq * 2, st));
+  if (vl) {
+    std::vector<int32_t> lcu(rows + 1);
+    for (int64_t r = 0; r <= rows; ++r) lcu[r] = (int32_t)(cu[row0 + r] - cu[row0]);
+    CUDA_CHECK(cudaMalloc(&dCu, (rows + 1) * 4));
+    CUDA_CHECK(cudaMemcpy(dCu, lcu.data(), (rows + 1) * 4, cudaMemcpyHostToDevice));
+  }
   auto launch = [&] {
-    FMHA_CHECK(fmha_forward_variant(dQ, dK, dV, dO, (int)rows, hq, hkv, s, d, o.variant, fs));
+    if (vl) {
+      FMHA_CHECK(fmha_forward_varlen(dQ, dK, dV, dO, static_cast<const int32_t*>(dCu), (int)rows,
+                                     hq, hkv, 16, d, 0.0f, fs));
+    } else {
+      FMHA_CHECK(fmha_forward_variant(dQ, dK, dV, dO, (int)rows, hq, hkv, s, d, o.variant, fs));
+    }
   };
   for (int i = 0; i < o.warmups; ++i) launch();
   CUDA_CHECK(cudaStreamSynchronize(st));
@@ -247,12 +269,18 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
 #pragma omp parallel for schedule(dynamic) reduction(+ : bad) reduction(max : max_abs, max_rel)
   for (size_t i = 0; i < pick.size(); ++i) {
     const int64_t r = pick[i], gr = row0 + r;
-    std::vector<uint16_t> q(hq * d), k((int64_t)hkv * s * d), v((int64_t)hkv * s * d);
+    const int sr = vl ? (int)(cu[gr + 1] - cu[gr]) : s;
+    const int64_t kv0 = vl ? cu[gr] * hkv * d : gr * hkv * s * d;  // first element of the row
+    std::vector<uint16_t> q(hq * d), k((int64_t)hkv * sr * d), v((int64_t)hkv * sr * d);
     gen_bf16(q.data(), hq * d, o.seed, 1, gr * hq * d);
-    gen_bf16(k.data(), (int64_t)hkv * s * d, o.seed, 2, gr * hkv * s * d);
-    gen_bf16(v.data(), (int64_t)hkv * s * d, o.seed, 3, gr * hkv * s * d);
+    gen_bf16(k.data(), (int64_t)hkv * sr * d, o.seed, 2, kv0);
+    gen_bf16(v.data(), (int64_t)hkv * sr * d, o.seed, 3, kv0);
     std::vector<float> ref((int64_t)hq * d);
-    cpu_row(q.data(), k.data(), v.data(), hq, hkv, s, d, ref.data());
+    if (vl) {
+      cpu_row(q.data(), k.data(), v.data(), hq, hkv, sr, d, d, (int64_t)hkv * d, ref.data());
+    } else {
+      cpu_row(q.data(), k.data(), v.data(), hq, hkv, sr, d, (int64_t)sr * d, d, ref.data());
+    }
     for (int64_t c = 0; c < (int64_t)hq * d; ++c) {
       const double got = f16_to_f32(hO[r * hq * d + c]);
       const double err = std::fabs(got - ref[c]);
@@ -273,6 +301,7 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
   cudaFree(dK);
   cudaFree(dV);
   cudaFree(dO);
+  if (dCu) cudaFree(dCu);
 }
 
 bool run_config(int idx, const Options& o) {
@@ -280,13 +309,24 @@ bool run_config(int idx, const Options& o) {
   const int hq = cfg.num_heads_q, hkv = cfg.num_heads_kv, d = cfg.head_dim, s = o.seqlen;
   const int n = std::max(1, std::min(o.gpus, cfg.batch));
   std::vector<ShardResult> res(n);
+  std::vector<int64_t> cu;
+  int64_t total_rows = (int64_t)cfg.batch * s;  // sum of K/V rows per head
+  if (o.varlen) {
+    // The reference benchmark's lengths: Poisson(4) in [2, 16], seed 42
+    // (fmha_host.cpp:58-72).
+    std::vector<int32_t> sl(cfg.batch);
+    FMHA_CHECK(fmha_seqlens_poisson(cfg.batch, 16, 42u, 4.0, sl.data()));
+    cu.assign(cfg.batch + 1, 0);
+    for (int b = 0; b < cfg.batch; ++b) cu[b + 1] = cu[b] + sl[b];
+    total_rows = cu[cfg.batch];
+  }
   std::vector<std::thread> th;
   HostBarrier bar;
   bar.n = n;
   for (int g = 0; g < n; ++g) {
     const int64_t r0 = (int64_t)cfg.batch * g / n, r1 = (int64_t)cfg.batch * (g + 1) / n;
-    th.emplace_back(run_shard, g, std::cref(cfg), std::cref(o), r0, r1 - r0, std::ref(bar),
-                    std::ref(res[g]));
+    th.emplace_back(run_shard, g, std::cref(cfg), std::cref(o), r0, r1 - r0, std::cref(cu),
+                    std::ref(bar), std::ref(res[g]));
   }
   for (auto& t : th) t.join();
 
@@ -304,8 +344,9 @@ bool run_config(int idx, const Options& o) {
   }
   const double b = cfg.batch;
   // Byte and flop formulas of fmha_host.cpp:413-414,428-431.
-  const double bytes = 2.0 * b * hq * d + 4.0 * b * hkv * s * d + 2.0 * b * hq * d;
-  const double flops = 4.0 * b * hq * s * d;
+  const double T = (double)total_rows;
+  const double bytes = 2.0 * b * hq * d + 4.0 * T * hkv * d + 2.0 * b * hq * d;
+  const double flops = 4.0 * hq * T * d;
   const double gbs = bytes / (ms * 1e-3) / 1e9;
   const double cpu_ms_per_row = checked ? cpu_sec * 1e3 / checked * n : 0;  // per-thread-set
   const int threads = omp_get_max_threads();
@@ -316,15 +357,23 @@ bool run_config(int idx, const Options& o) {
         "\"num_heads_kv\": %d, \"seqlen_kv\": %d, \"head_dim\": %d, \"gpus\": %d, "
         "\"us_per_call\": %.3f, \"gbs\": %.1f, \"tflops\": %.3f, \"rows_checked\": %lld, "
         "\"bad\": %lld, \"max_abs_err\": %.3e, \"max_rel_err\": %.3e, \"cpu_ms_per_row\": %.4f, "
-        "\"cpu_threads\": %d, \"device_error\": %d, \"passed\": %s}\n",
-        idx, cfg.note, cfg.batch, hq, hkv, s, d, n, ms * 1e3, gbs, flops / (ms * 1e-3) / 1e12,
+        "\"cpu_threads\": %d, \"device_error\": %d, \"varlen\": %s, \"passed\": %s}\n",
+        idx, cfg.note, cfg.batch, hq, hkv, o.varlen ? -1 : s, d, n, ms * 1e3, gbs,
+        flops / (ms * 1e-3) / 1e12,
         (long long)checked, (long long)bad, max_abs, max_rel, cpu_ms_per_row, threads, dev_err,
-        ok ? "true" : "false");
+        o.varlen ? "true" : "false", ok ? "true" : "false");
   } else {
     std::printf("\n=== Configuration %d (%s) ===\n", idx, cfg.note);
-    std::printf("  Batch %d, heads Q %d, heads KV %d (%s), seqlen_q 1, seqlen_kv %d, head_dim %d\n",
-                cfg.batch, hq, hkv, hq == hkv ? "MHA" : "GQA", s, d);
-    std::printf("  Layout Q/O [B,H,1,D], K/V [B,Hkv,S,D]; bf16 in, fp32 softmax, fp16 out\n");
+    if (o.varlen) {
+      std::printf("  Batch %d, heads Q %d, heads KV %d (%s), seqlen_q 1, seqlen_kv Poisson(4) in "
+                  "[2,16], avg %.3f, head_dim %d\n",
+                  cfg.batch, hq, hkv, hq == hkv ? "MHA" : "GQA", T / b, d);
+      std::printf("  Layout Q/O [B,H,1,D], K/V packed [sum S,Hkv,D] + cu_seqlens_kv\n");
+    } else {
+      std::printf("  Batch %d, heads Q %d, heads KV %d (%s), seqlen_q 1, seqlen_kv %d, head_dim %d\n",
+                  cfg.batch, hq, hkv, hq == hkv ? "MHA" : "GQA", s, d);
+      std::printf("  Layout Q/O [B,H,1,D], K/V [B,Hkv,S,D]; bf16 in, fp32 softmax, fp16 out\n");
+    }
     std::printf("  GPUs %d (batch shards of ~%d rows, no collective)\n", n, cfg.batch / n);
     std::printf("Average time:  %.4f ms per iteration (slowest GPU)\n", ms);
     std::printf("Throughput:    %.1f iter/s\n", 1000.0 / ms);
@@ -343,7 +392,7 @@ void usage() {
   std::fprintf(stderr,
                "usage: fmha_host [config_index 0..%d] [--all] [--gpus N] [--iters N] "
                "[--warmups N] [--seqlen 1..16] [--seed S] [--variant auto|bulk|ldg] "
-               "[--validate-rows N] [--json]\n",
+               "[--validate-rows N] [--json] [--varlen]\n",
                kNumConfigs - 1);
 }
 
@@ -369,6 +418,7 @@ int main(int argc, char** argv) {
     else if (a == "--seed") o.seed = std::strtoull(next("--seed"), nullptr, 10);
     else if (a == "--validate-rows") o.validate_rows = std::atoi(next("--validate-rows"));
     else if (a == "--json") o.json = true;
+    else if (a == "--varlen") o.varlen = true;
     else if (a == "--variant") {
       std::string v = next("--variant");
       o.variant = v == "bulk" ? FMHA_VARIANT_BULK : v == "ldg" ? FMHA_VARIANT_LDG

@@ -105,6 +105,26 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V,
                                   int max_seqlen_kv, int head_dim,
                                   float softmax_scale, fmha_stream_t stream);
 
+/*
+ * fmha_forward_append -- one decode step with a KV cache: writes this step's
+ * K/V rows into the cache and attends over the whole prefix, in one kernel.
+ *   K_cache, V_cache [batch, num_heads_kv, cache_seqlen, head_dim] bf16; rows
+ *     0..seqlen_kv-2 hold the earlier steps (read), row seqlen_kv-1 is
+ *     written from K_new / V_new;
+ *   K_new, V_new [batch, num_heads_kv, 1, head_dim] bf16 (this step);
+ *   Q, O as in fmha_forward.
+ * O equals fmha_forward on the first seqlen_kv rows of the updated cache
+ * (the new row is taken from K_new/V_new directly, not re-read). seqlen_kv in
+ * 1..16, cache_seqlen >= seqlen_kv. No reference counterpart: the reference
+ * benchmark has no cache update; this is the producer side of its decode
+ * step.
+ */
+fmha_status_t fmha_forward_append(const void* Q, void* K_cache, void* V_cache,
+                                  const void* K_new, const void* V_new, void* O,
+                                  int batch, int num_heads_q, int num_heads_kv,
+                                  int seqlen_kv, int cache_seqlen, int head_dim,
+                                  fmha_stream_t stream);
+
 /* Human-readable name of a status code (static storage). Reference
  * counterpart: the HIP_CHECK error text (fmha_host.cpp:26-35). */
 const char* fmha_status_string(fmha_status_t status);

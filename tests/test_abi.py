@@ -130,3 +130,14 @@ def test_seqlens_poisson_matches_reference_generator(oracle):
         pytest.skip("reference build absent")
     assert np.array_equal(got, oracle.ref_generate_seqlens(30720, 16))
     assert np.array_equal(fmha_b200.seqlens_poisson(100, 8), oracle.ref_generate_seqlens(100, 8))
+
+
+def test_compat_header_compiles_on_cpu(tmp_path):
+    """include/fmha_compat.hpp is valid C++ for a host compiler (the reference
+    call site's translation unit)."""
+    import shutil
+    import subprocess
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    src = os.path.join(ROOT, "tests", "cpp", "compat_call.cpp")
+    subprocess.check_call([nvcc, "-std=c++17", "-I" + os.path.join(ROOT, "include"), "-c", src,
+                           "-o", str(tmp_path / "c.o")])

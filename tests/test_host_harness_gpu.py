@@ -14,7 +14,9 @@ BIN = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), 
 
 
 @pytest.mark.parametrize("args", [["0"], ["5", "--seqlen", "7", "--validate-rows", "16"],
-                                  ["0", "--variant", "bulk", "--seqlen", "1"]])
+                                  ["0", "--variant", "bulk", "--seqlen", "1"],
+                                  ["0", "--varlen"], ["4", "--varlen", "--validate-rows", "16"],
+                                  ["5", "--varlen", "--validate-rows", "16"]])
 def test_fmha_host_validates(cuda, args):
     if not os.path.exists(BIN):
         pytest.fail("fmha_host was not built (python -m fmha_b200.build)")
