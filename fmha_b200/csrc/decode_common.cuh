@@ -389,6 +389,26 @@ struct Tile16 {
   static_assert(G % GB == 0, "GB");
 };
 
+// q . k over 8 bf16 pairs with mixed-precision FMAs (bf16 operands, fp32
+// accumulator, sm_100): the bf16 x bf16 product is exact in fp32, so this
+// rounds exactly like unpacking both to fp32 and chaining fmaf in the same
+// order, without the unpack instructions.
+__device__ __forceinline__ float dot8_bf16(const uint4 q, const uint4 k) {
+  float a = 0.0f;
+  asm("{\n\t.reg .b16 q0, q1, k0, k1;\n\t"
+      "mov.b32 {q0, q1}, %1;\n\tmov.b32 {k0, k1}, %5;\n\t"
+      "fma.rn.f32.bf16 %0, q0, k0, %0;\n\tfma.rn.f32.bf16 %0, q1, k1, %0;\n\t"
+      "mov.b32 {q0, q1}, %2;\n\tmov.b32 {k0, k1}, %6;\n\t"
+      "fma.rn.f32.bf16 %0, q0, k0, %0;\n\tfma.rn.f32.bf16 %0, q1, k1, %0;\n\t"
+      "mov.b32 {q0, q1}, %3;\n\tmov.b32 {k0, k1}, %7;\n\t"
+      "fma.rn.f32.bf16 %0, q0, k0, %0;\n\tfma.rn.f32.bf16 %0, q1, k1, %0;\n\t"
+      "mov.b32 {q0, q1}, %4;\n\tmov.b32 {k0, k1}, %8;\n\t"
+      "fma.rn.f32.bf16 %0, q0, k0, %0;\n\tfma.rn.f32.bf16 %0, q1, k1, %0;\n\t}"
+      : "+f"(a)
+      : "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w), "r"(k.x), "r"(k.y), "r"(k.z), "r"(k.w));
+  return a;
+}
+
 __device__ __forceinline__ float dot8f(const float (&q)[8], const float (&k)[8]) {
   float a = q[0] * k[0];
 #pragma unroll
@@ -421,24 +441,17 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
 #pragma unroll
     for (int us = 0; us < T::LU; ++us) {
       const int u = slot_unit(us);
-      float q[T::GB][8];
+      uint4 q[T::GB];
 #pragma unroll
-      for (int g = 0; g < T::GB; ++g) {
-        if (u < units_valid) {
-          unpack8(loadQ(us, u, gb + g), q[g]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) q[g][c] = 0.0f;
-        }
-      }
+      for (int g = 0; g < T::GB; ++g)
+        q[g] = u < units_valid ? loadQ(us, u, gb + g) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int i = 0; i < T::SPL; ++i) {
         const int p = us * T::SPL + i;
         if (row_ok(p)) {
-          float kf[8];
-          unpack8(loadK(p), kf);
+          const uint4 k = loadK(p);
 #pragma unroll
-          for (int g = 0; g < T::GB; ++g) v[g][p] = dot8f(q[g], kf);
+          for (int g = 0; g < T::GB; ++g) v[g][p] = dot8_bf16(q[g], k);
         } else {
 #pragma unroll
           for (int g = 0; g < T::GB; ++g) v[g][p] = 0.0f;
