@@ -288,8 +288,10 @@ __device__ __forceinline__ float reduce_scatter(float (&v)[N], int cl) {
 //
 // Math per (unit, head): x_s = (q . k_s) * log2(e)/sqrt(D) for s < s_len
 // (-inf beyond, the reference's max_seqlen 16 tile masking); p_s =
-// 2^(x_s - max) / sum; o = sum_s p_s v_s. P stays fp32 (the reference's
-// vectorized kernel keeps fp32 P, fmha_vectorized_fma_kernel.hpp:256,281-287;
+// 2^(x_s - max) / sum; o = sum_s p_s v_s. Non-finite inputs behave as in the
+// reference (fmha_host.cpp:215-226): a NaN score or a head whose scores are
+// all -inf gives NaN weights; only an empty row (s_len == 0) yields zeros.
+// P stays fp32 (the reference's vectorized kernel keeps fp32 P, fmha_vectorized_fma_kernel.hpp:256,281-287;
 // its host oracle rounds P to bf16, fmha_host.cpp:225, which the fp16-output
 // tolerance of this library does not allow).
 template <int D, int SMAX, int G, class LoadK, class LoadV>
@@ -328,11 +330,11 @@ __device__ __forceinline__ void attend_tile(const float (&q)[G][8], LoadK loadK,
     float m = x;
 #pragma unroll
     for (int o = 1; o < SMAX; o <<= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
-    const float ex = (m == -INFINITY) ? 0.0f : exp2f(x - m);
+    const float ex = s_len == 0 ? 0.0f : exp2f(x - m);
     float sum = ex;
 #pragma unroll
     for (int o = 1; o < SMAX; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
-    if (e < T::SC) sc[e] = sum > 0.0f ? ex / sum : 0.0f;
+    if (e < T::SC) sc[e] = s_len == 0 ? 0.0f : ex / sum;
   }
   __syncwarp();
 
@@ -475,11 +477,11 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
     float m = x;
 #pragma unroll
     for (int o = 1; o < SMAX; o <<= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
-    const float ex = (m == -INFINITY) ? 0.0f : exp2f(x - m);
+    const float ex = s_len == 0 ? 0.0f : exp2f(x - m);
     float sum = ex;
 #pragma unroll
     for (int o = 1; o < SMAX; o <<= 1) sum += __shfl_xor_sync(kFullMask, sum, o);
-    if (e < T::SC) sc[e] = sum > 0.0f ? ex / sum : 0.0f;
+    if (e < T::SC) sc[e] = s_len == 0 ? 0.0f : ex / sum;
   }
   __syncwarp();
 
