@@ -141,3 +141,17 @@ def test_compat_header_compiles_on_cpu(tmp_path):
     src = os.path.join(ROOT, "tests", "cpp", "compat_call.cpp")
     subprocess.check_call([nvcc, "-std=c++17", "-I" + os.path.join(ROOT, "include"), "-c", src,
                            "-o", str(tmp_path / "c.o")])
+
+
+def test_oversized_unit_count_is_rejected():
+    """More than 2**30 (batch, kv head) units is outside the kernels' int32
+    chunk indexing: rejected up front, not truncated."""
+    assert call(batch=1 << 26, num_heads_q=32, num_heads_kv=32) == _lib.FMHA_ERR_UNSUPPORTED
+
+
+def test_append_rejects_bad_new_rows():
+    lib = fmha_b200.load()
+    args = [16, 32, 48, None, 80, 96, 2, 16, 16, 8, 8, 128, None]
+    assert lib.fmha_forward_append(*args) == _lib.FMHA_ERR_INVALID_ARG
+    args[3] = 72
+    assert lib.fmha_forward_append(*args) == _lib.FMHA_ERR_MISALIGNED
