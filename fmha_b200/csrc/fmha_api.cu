@@ -120,7 +120,9 @@ int rows_per_access(int d) { return 256 / d; }
 // (D=256, S=16, one query head per kv head) and for D=128, S=1; elsewhere the
 // bulk ring wins, with ~10 consumer warps for 8-16 row units (leaving ring
 // stages for copies in flight) and 16 for short units (more tiles per stage).
-// FMHA_VARIANT (1 bulk, 2 ldg) and FMHA_BULK_WARPS override the table.
+// With 4 or 8 query heads per kv head the choice flips for D=256 short rows
+// (ldg) and D=128 long rows (16 warps). FMHA_VARIANT (1 bulk, 2 ldg) and
+// FMHA_BULK_WARPS override the table.
 struct Choice {
   int variant;
   int warps;
@@ -129,7 +131,13 @@ struct Choice {
 Choice auto_choice(int d, int smax, int g) {
   static const int forced = env_int("FMHA_VARIANT", 0);
   Choice c{FMHA_VARIANT_BULK, 16};
-  if (d == 256 && smax == 16 && g == 1) c = {FMHA_VARIANT_LDG, 0};
+  if (g >= 4) {
+    // 4 or 8 query heads per kv head (measured separately).
+    if (d == 128) c = smax <= 2 ? Choice{FMHA_VARIANT_LDG, 0} : Choice{FMHA_VARIANT_BULK, 16};
+    else if (smax >= 8) c = {FMHA_VARIANT_BULK, 10};
+    else if (g == 4 && smax == 1) c = {FMHA_VARIANT_BULK, 10};
+    else c = {FMHA_VARIANT_LDG, 0};
+  } else if (d == 256 && smax == 16 && g == 1) c = {FMHA_VARIANT_LDG, 0};
   else if (d == 128 && smax == 1 && g == 1) c = {FMHA_VARIANT_LDG, 0};
   else if (smax >= 8) c = {FMHA_VARIANT_BULK, 10};
   else if (d == 128 && smax == 4) c = {FMHA_VARIANT_BULK, 8};
