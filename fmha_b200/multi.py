@@ -52,3 +52,46 @@ def gather_output(local_o, shard: Shard, group=None):
     dist.all_gather(parts, buf, group=group)
     out = torch.cat([p[:int(s.item())] for p, s in zip(parts, sizes)])
     return out.view(local_o.dtype)
+
+
+class ShardMonitor:
+    """Host-side failure detection for the batch-sharded driver.
+
+    Each rank posts its status for every step to a torch.distributed store
+    (TCPStore; key "fmha/<step>/<rank>" = "ok" or "fail:<reason>") *between*
+    steps, never while its kernels are in flight. ``wait_step`` collects the
+    statuses of all ranks for a step with a bounded wait and returns the ranks
+    that reported a failure and the ranks that never reported, so a driver can
+    stop cleanly instead of blocking in a collective. Nothing here touches a
+    GPU.
+    """
+
+    def __init__(self, store, rank: int, world: int, prefix: str = "fmha"):
+        self.store, self.rank, self.world, self.prefix = store, rank, world, prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def report(self, step: int, ok: bool = True, reason: str = "") -> None:
+        self.store.set(self._key(step, self.rank), "ok" if ok else f"fail:{reason}")
+
+    def wait_step(self, step: int, timeout_s: float = 5.0, poll_s: float = 0.01):
+        """Returns (failed: {rank: reason}, missing: [rank]) for ``step``."""
+        import time
+        deadline = time.monotonic() + timeout_s
+        failed, seen = {}, set()
+        while True:
+            for r in range(self.world):
+                if r in seen:
+                    continue
+                key = self._key(step, r)
+                if self.store.check([key]):
+                    v = self.store.get(key).decode()
+                    seen.add(r)
+                    if v != "ok":
+                        failed[r] = v[len("fail:"):]
+            if len(seen) == self.world or time.monotonic() >= deadline:
+                break
+            time.sleep(poll_s)
+        missing = [r for r in range(self.world) if r not in seen]
+        return failed, missing

@@ -63,3 +63,54 @@ def test_gloo_two_rank_shards_equal_single_process(tmp_path, oracle):
         got = np.load(tmp_path / f"r{r}.npy").view(np.uint16)
         assert np.array_equal(got, ref)
         assert float(np.load(tmp_path / f"m{r}.npy")[0]) == world
+
+
+def _fault_worker(rank, world, port, outdir, mode):
+    """Rank 1 misbehaves after step 0: it reports a failure ("raise") or
+    stops reporting ("silent"). The other ranks must learn of it through the
+    store within the bounded wait and stop before the next step."""
+    import datetime
+    import json
+    from fmha_b200.multi import ShardMonitor
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=20))
+    mon = ShardMonitor(store, rank, world, prefix=f"t-{mode}")
+    log = []
+    for step in range(3):
+        if rank == 1 and step == 1:
+            if mode == "raise":
+                try:
+                    raise RuntimeError("injected shard failure")
+                except RuntimeError as e:
+                    mon.report(step, ok=False, reason=str(e))
+            log.append(("stopped", step))
+            break  # leaves between steps, nothing in flight
+        mon.report(step, ok=True)
+        failed, missing = mon.wait_step(step, timeout_s=1.0)
+        log.append((step, sorted(failed), missing))
+        if failed or missing:
+            break
+    with open(os.path.join(outdir, f"f{mode}{rank}.json"), "w") as f:
+        json.dump(log, f)
+    if rank == 0:
+        import time
+        time.sleep(0.5)  # keep the store up while the others read
+
+
+@pytest.mark.parametrize("mode", ["raise", "silent"])
+def test_shard_failure_is_detected_on_the_host(tmp_path, mode):
+    import json
+    world = 3
+    mp.spawn(_fault_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world,
+             join=True)
+    for r in (0, 2):
+        log = json.load(open(tmp_path / f"f{mode}{r}.json"))
+        assert log[0] == [0, [], []]
+        step, failed, missing = log[1]
+        assert step == 1
+        if mode == "raise":
+            assert failed == [1] and missing == []
+        else:
+            assert failed == [] and missing == [1]
+        assert len(log) == 2  # stopped before step 2
+    assert json.load(open(tmp_path / f"f{mode}1.json"))[-1] == ["stopped", 1]
