@@ -290,6 +290,8 @@ def main():
                     help="skip the nvidia-smi sampler (profiling runs)")
     ap.add_argument("--varlen-uniform", type=int, default=0,
                     help="varlen configs: every row this long instead of Poisson(4) (profiling)")
+    ap.add_argument("--varlen-mix", default="",
+                    help="varlen configs: rows cycle through these lengths, e.g. 3,4 (profiling)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (small profiling cases only)")
     ap.add_argument("--sweep", action="store_true",
@@ -486,6 +488,9 @@ def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_rank
     sl_all = fmha_b200.seqlens_poisson(b_all, max_s, 42, 4.0)
     if args.varlen_uniform > 0:
         sl_all[:] = args.varlen_uniform
+    if args.varlen_mix:
+        mix = np.array([int(x) for x in args.varlen_mix.split(",")], dtype=np.int32)
+        sl_all[:] = np.resize(mix, b_all)
     lo, hi = shard(b_all, world, rank)
     b = hi - lo
     cu_all = np.concatenate([[0], np.cumsum(sl_all)]).astype(np.int64)

@@ -574,7 +574,7 @@ VarlenFn varlen_ring_kernel_d256(int g);
 VarlenFn varlen_chunk_kernel_d128(int g);
 VarlenFn varlen_chunk_kernel_d256(int g);
 constexpr int kVarlenSlots = 32;           // chunk descriptors in flight per CTA
-constexpr uint32_t kVarlenChunkHdr = 4096;  // barriers, counters, descriptors
+constexpr uint32_t kVarlenChunkHdr = 8192;  // barriers, counters, descriptors
 constexpr uint32_t kVarlenDescBytes = 64;
 constexpr int kVarlenProducers = 6;  // default gathering warps per varlen ring CTA
 

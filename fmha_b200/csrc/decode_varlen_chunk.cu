@@ -6,17 +6,24 @@
 //
 // In the packed layout the K rows of one batch row b, all kv heads, are one
 // contiguous block of S_b*Hkv*D elements (so are its V rows, and its Hq query
-// rows). A *chunk* is that block -- or, when a row is too long for the chunk
-// limit, the rows of a group of nh consecutive kv heads, whose K rows at one
-// position s are one contiguous run of nh*D elements.
+// rows), and consecutive batch rows are adjacent. A *chunk* is up to
+// kChunkRows consecutive whole rows (three contiguous ranges: K, V, Q) that
+// fit the chunk limit -- or, for a row too long for the limit on its own, the
+// rows of a group of nh consecutive kv heads, whose K rows at one position s
+// are one contiguous run of nh*D elements. Packing short rows together keeps
+// every chunk large, which is what keeps the bulk copies efficient.
 //
 // Per CTA (persistent, one per SM): a contiguous range of batch rows.
 //  * Producer (warp 0) walks the rows in order (cu_seqlens read 31 rows per
-//    warp load), allocates each chunk in a circular byte ring (a chunk never
-//    wraps: the tail skips to the ring start instead), writes the chunk's
-//    descriptor into slot c % kSlots, arms the slot's `full` mbarrier with the
-//    chunk's byte count and issues the copies: one bulk copy each for K, V and
-//    Q of a whole row, or one K and one V copy per position for a head group.
+//    warp load), allocates each chunk in a circular byte ring whose size is a
+//    multiple of one row (D*2 bytes), so a chunk may wrap past the end
+//    without any row straddling it (copies that cross are split in two;
+//    readers wrap their row offsets), and no space is lost to padding; writes
+//    the chunk's
+//    descriptor (per-row lengths, offsets and first tiles) into slot
+//    c % kSlots, arms the slot's `full` mbarrier with the chunk's byte count
+//    and issues the copies: one bulk copy each for K, V and Q of whole rows,
+//    or one K and one V copy per position for a head group.
 //    It then publishes the chunk count. Ring space and slots are reclaimed in
 //    chunk order by waiting on each slot's `empty` mbarrier, one phase after
 //    another (a single producer walks every slot's phases in order).
@@ -43,44 +50,59 @@ namespace fmha {
 
 namespace {
 
-struct ChunkDesc {
-  int64_t b;          // batch row
+constexpr int kChunkRows = 8;  // whole batch rows per chunk at most
+
+struct alignas(16) ChunkDesc {
+  int64_t b0;         // first batch row
   int64_t end_total;  // ring bytes allocated up to the end of this chunk
   uint32_t off;       // chunk start in the ring
-  uint32_t kv_bytes;  // bytes of the K block (= of the V block)
-  int s_len;          // rows per head
-  int smax;           // power of two >= s_len
-  int h0;             // first kv head of the chunk
-  int nh;             // kv heads in the chunk
+  uint32_t kv_bytes;  // bytes of the K part (= of the V part)
+  int h0;             // first kv head covered
+  int nh;             // kv heads covered (all rows of the chunk)
   int tile_base;      // CTA-local index of the chunk's first tile
   int ntiles;
+  int nrows;
+  int pad;
+  uint16_t krow[kChunkRows];    // first K/V row of row j, relative to the chunk
+  uint16_t s_len[kChunkRows];   // rows per head of row j
+  uint16_t tstart[kChunkRows];  // tiles of rows < j
 };
-static_assert(sizeof(ChunkDesc) == 48, "descriptor size");
+static_assert(sizeof(ChunkDesc) <= 112, "descriptor size");
+constexpr uint32_t kDescStride = 112;
+
+// What one tile needs: its batch row, length, heads and shared-memory bases.
+struct TileRef {
+  int64_t b;
+  int s_len;
+  int h0;         // first kv head of the chunk
+  int nh;         // row stride in heads inside the chunk
+  uint32_t koff, voff, qoff;  // ring-relative offsets (< R); rows wrap at R
+};
 
 __device__ __forceinline__ int smax_of(int s) {
   return s <= 1 ? 1 : s <= 2 ? 2 : s <= 4 ? 4 : s <= 8 ? 8 : 16;
 }
 
 template <int D, int SMAX, int G>
-__device__ __forceinline__ void chunk_tile(const VarlenParams& P, const ChunkDesc& c, int hl0,
-                                           uint32_t cbase, float* sc, int lane) {
+__device__ __forceinline__ void chunk_tile(const VarlenParams& P, const TileRef& c, int hl0,
+                                           uint32_t ring0, uint32_t R, float* sc, int lane) {
   using T = Tile16<D, SMAX, G>;
   const int r0 = lane / T::LPR;
   const int cl = lane % T::LPR;
   const int nh = c.nh;
   const int nv = nh - hl0 < T::NU ? nh - hl0 : T::NU;
-  const uint32_t kl = cbase + cl * 16;
-  const uint32_t vl = kl + c.kv_bytes;
-  const uint32_t ql = cbase + 2 * c.kv_bytes + cl * 16;
+  // Ring addresses wrap at R (a multiple of the row size, so a row never
+  // straddles the end).
+  auto at = [&](uint32_t off) { return ring0 + (off >= R ? off - R : off) + cl * 16; };
   // Tile row r = (unit u, position s) is chunk row s*nh + hl0 + u.
   auto rowoff = [&](int p) -> uint32_t {
     const int r = r0 * T::NP + p;
     return (uint32_t)((r % SMAX) * nh + hl0 + r / SMAX) * (D * 2);
   };
-  auto loadK = [&](int p) { return lds128(kl + rowoff(p)); };
-  auto loadV = [&](int p) { return lds128(vl + rowoff(p)); };
+  auto loadK = [&](int p) { return lds128(at(c.koff + rowoff(p))); };
+  auto loadV = [&](int p) { return lds128(at(c.voff + rowoff(p))); };
   auto loadQ = [&](int, int u, int g) {
-    return lds128(ql + (uint32_t)((hl0 + u) * G + g) * (D * 2));
+    return lds128(at(c.qoff + (uint32_t)((hl0 + u) * G + g) * (D * 2)));
   };
   const int64_t qrow0 = (c.b * P.num_heads_kv + c.h0 + hl0) * G;
   auto store = [&](int u, const float (&acc)[G][8]) {
@@ -109,10 +131,13 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
   volatile int* total_tiles = ctrl + 2;  // tile count once the producer is done, else -1
   int* next_tile = const_cast<int*>(ctrl + 3);
   int* done = const_cast<int*>(ctrl + 4);  // [M] tiles finished per slot
-  ChunkDesc* desc = reinterpret_cast<ChunkDesc*>(smem + 16 * M + 4 * (4 + M));
+  unsigned char* desc_base = smem + ((16 * M + 4 * (4 + M) + 15) & ~15);
+  auto desc_at = [&](int slot) {
+    return reinterpret_cast<ChunkDesc*>(desc_base + (size_t)slot * kDescStride);
+  };
   unsigned char* ring = smem + P.ring_off;
   const uint32_t ring0 = smem_u32(ring);
-  const uint32_t R = P.stage_bytes;  // ring size in bytes (multiple of 128)
+  const uint32_t R = P.stage_bytes;  // ring size in bytes (a multiple of the row size D*2)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < M; ++i) {
@@ -138,6 +163,89 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
     int64_t tail = 0, head = 0;  // ring bytes ever allocated / ever released
     int c = 0, oldest = 0, tiles = 0;
     bool stop = false;
+    auto heads_per_tile = [](int s_len) {
+      const int s = s_len <= 1 ? 1 : s_len <= 2 ? 2 : s_len <= 4 ? 4 : s_len <= 8 ? 8 : 16;
+      return 16 / s;
+    };
+    // Pending multi-row chunk; lane j keeps row j's length, relative K row
+    // and first tile.
+    int pn = 0, p_rows = 0, p_tiles = 0, p_c0 = 0;
+    int64_t p_b0 = 0;
+    int my_s = 0, my_krow = 0, my_tstart = 0;
+
+    // Allocates ring space and a slot for a chunk, writes its descriptor
+    // (lanes j < nrows write their row entries), arms `full` and publishes
+    // the chunk after `issue` has launched its copies.
+    auto emit = [&](int64_t b0, int nrows, int h0, int nh, int ntiles, uint32_t kvb,
+                    uint32_t qb, int s_row, int krow, int tstart, auto&& issue) {
+      const uint32_t sz = 2 * kvb + qb;  // whole rows: a multiple of D*2 bytes
+      while (oldest <= c - M || tail + sz - head > (int64_t)R) {
+        if (!mbar_wait(empty0 + 8u * (oldest % M), (oldest / M) & 1, abort_flag, P.err,
+                       P.wait_timeout_ns, kSiteProducerEmpty)) {
+          stop = true;
+          return;
+        }
+        head = desc_at(oldest % M)->end_total;
+        ++oldest;
+      }
+      const uint32_t off = (uint32_t)(tail % R);
+      tail += sz;
+      const int slot = c % M;
+      const uint32_t bar = full0 + 8u * slot;
+      ChunkDesc* d = desc_at(slot);
+      if (lane < nrows) {
+        d->krow[lane] = (uint16_t)krow;
+        d->s_len[lane] = (uint16_t)s_row;
+        d->tstart[lane] = (uint16_t)tstart;
+      }
+      if (lane == 0) {
+        d->b0 = b0;
+        d->end_total = tail;
+        d->off = off;
+        d->kv_bytes = kvb;
+        d->h0 = h0;
+        d->nh = nh;
+        d->tile_base = tiles;
+        d->ntiles = ntiles;
+        d->nrows = nrows;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(bar, 2 * kvb + qb);  // releases the descriptor
+      __syncwarp();
+      issue(off, bar);
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        *published = c + 1;
+      }
+      tiles += ntiles;
+      ++c;
+    };
+
+    // Bulk copy of len bytes to ring offset off (< R), split in two where it
+    // runs past the end of the ring.
+    auto copy_to_ring = [&](uint32_t off, const uint16_t* src, uint32_t len, uint32_t bar) {
+      if (off >= R) off -= R;
+      const uint32_t first = off + len > R ? R - off : len;
+      bulk_g2s(ring0 + off, src, first, bar, policy);
+      if (first < len) bulk_g2s(ring0, src + first / 2, len - first, bar, policy);
+    };
+
+    auto flush = [&]() {
+      if (pn == 0 || stop) return;
+      const uint32_t kvb = (uint32_t)p_rows * hkv * (D * 2);
+      const uint32_t qb = (uint32_t)(pn * hkv * G) * (D * 2);
+      const int64_t ksrc = (int64_t)p_c0 * hkv * D;
+      const int64_t qsrc = p_b0 * hkv * G * D;
+      emit(p_b0, pn, 0, hkv, p_tiles, kvb, qb, my_s, my_krow, my_tstart,
+           [&](uint32_t dst, uint32_t bar) {
+             if (lane == 0 && kvb) copy_to_ring(dst, P.K + ksrc, kvb, bar);
+             if (lane == 1 && kvb) copy_to_ring(dst + kvb, P.V + ksrc, kvb, bar);
+             if (lane == 2) copy_to_ring(dst + 2 * kvb, P.Q + qsrc, qb, bar);
+           });
+      pn = p_rows = p_tiles = 0;
+    };
+
     for (int64_t base = row_lo; base < row_hi && !stop; base += 31) {
       const int64_t idx = base + lane;
       const int cu_l = idx <= row_hi ? __ldg(P.cu_seqlens + idx) : 0;
@@ -147,81 +255,57 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
         const int s_len = __shfl_sync(kFullMask, cu_l, i + 1) - c0;
         const int64_t b = base + i;
         if (s_len < 0 || s_len > P.max_seqlen) {
+          flush();  // chunks hold consecutive rows only
           if (lane == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
           continue;
         }
-        const int smax = smax_of(s_len);
-        const int nu = 16 / smax;
+        const int nu = heads_per_tile(s_len);
         const uint32_t per_head = (uint32_t)(2 * s_len + G) * (D * 2);
+        const uint32_t row_bytes = per_head * hkv;
+        if (row_bytes <= P.chunk_max) {
+          // Whole row: append to the pending chunk (flush first if full).
+          const uint32_t pend = (uint32_t)(2 * p_rows + pn * G) * hkv * (D * 2);
+          if (pn == kChunkRows || (pn > 0 && pend + row_bytes > P.chunk_max)) flush();
+          if (stop) break;
+          if (pn == 0) {
+            p_b0 = b;
+            p_c0 = c0;
+          }
+          if (lane == pn) {
+            my_s = s_len;
+            my_krow = c0 - p_c0;
+            my_tstart = p_tiles;
+          }
+          ++pn;
+          p_rows += s_len;
+          p_tiles += (hkv + nu - 1) / nu;
+          continue;
+        }
+        // Row too long on its own: head groups with one copy per position.
+        flush();
         int nh_max = (int)(P.chunk_max / per_head);
         if (nh_max < 1) nh_max = 1;
         if (nh_max > hkv) nh_max = hkv;
-        if (nh_max < hkv && nh_max >= nu) nh_max -= nh_max % nu;  // whole tiles per group
+        if (nh_max >= nu) nh_max -= nh_max % nu;  // whole tiles per group
         for (int h0 = 0; h0 < hkv && !stop; h0 += nh_max) {
           const int nh = hkv - h0 < nh_max ? hkv - h0 : nh_max;
           const uint32_t kvb = (uint32_t)s_len * nh * (D * 2);
           const uint32_t qb = (uint32_t)(nh * G) * (D * 2);
-          const uint32_t sz = (2 * kvb + qb + 127u) & ~127u;
-          const uint32_t pos = (uint32_t)(tail % R);
-          const uint32_t pad = pos + sz > R ? R - pos : 0u;
-          // Reclaim chunks in order until the slot is free and the bytes fit.
-          while (oldest <= c - M || tail + pad + sz - head > (int64_t)R) {
-            if (!mbar_wait(empty0 + 8u * (oldest % M), (oldest / M) & 1, abort_flag, P.err,
-                           P.wait_timeout_ns, kSiteProducerEmpty)) {
-              stop = true;
-              break;
-            }
-            head = desc[oldest % M].end_total;
-            ++oldest;
-          }
-          if (stop) break;
-          const int64_t start = tail + pad;
-          const uint32_t off = (uint32_t)(start % R);
-          tail = start + sz;
-          const int nt = (nh + nu - 1) / nu;
-          const int slot = c % M;
-          const uint32_t bar = full0 + 8u * slot;
-          if (lane == 0) {
-            ChunkDesc& d = desc[slot];
-            d.b = b;
-            d.end_total = tail;
-            d.off = off;
-            d.kv_bytes = kvb;
-            d.s_len = s_len;
-            d.smax = smax;
-            d.h0 = h0;
-            d.nh = nh;
-            d.tile_base = tiles;
-            d.ntiles = nt;
-            mbar_arrive_expect_tx(bar, 2 * kvb + qb);
-          }
-          __syncwarp();
-          const uint32_t dst = ring0 + off;
+          const uint32_t run = (uint32_t)nh * (D * 2);
           const int64_t qsrc = (b * hkv + h0) * G * D;
-          if (nh == hkv) {
-            const int64_t ksrc = (int64_t)c0 * hkv * D;
-            if (lane == 0 && kvb) bulk_g2s(dst, P.K + ksrc, kvb, bar, policy);
-            if (lane == 1 && kvb) bulk_g2s(dst + kvb, P.V + ksrc, kvb, bar, policy);
-            if (lane == 2) bulk_g2s(dst + 2 * kvb, P.Q + qsrc, qb, bar, policy);
-          } else {
-            const uint32_t run = (uint32_t)nh * (D * 2);
-            if (lane < s_len) {
-              const int64_t ksrc = ((int64_t)(c0 + lane) * hkv + h0) * D;
-              bulk_g2s(dst + lane * run, P.K + ksrc, run, bar, policy);
-              bulk_g2s(dst + kvb + lane * run, P.V + ksrc, run, bar, policy);
-            }
-            if (lane == 31) bulk_g2s(dst + 2 * kvb, P.Q + qsrc, qb, bar, policy);
-          }
-          __syncwarp();
-          if (lane == 0) {
-            __threadfence_block();
-            *published = c + 1;
-          }
-          tiles += nt;
-          ++c;
+          emit(b, 1, h0, nh, (nh + nu - 1) / nu, kvb, qb, s_len, 0, 0,
+               [&](uint32_t dst, uint32_t bar) {
+                 if (lane < s_len) {
+                   const int64_t ksrc = ((int64_t)(c0 + lane) * hkv + h0) * D;
+                   copy_to_ring(dst + lane * run, P.K + ksrc, run, bar);
+                   copy_to_ring(dst + kvb + lane * run, P.V + ksrc, run, bar);
+                 }
+                 if (lane == 31) copy_to_ring(dst + 2 * kvb, P.Q + qsrc, qb, bar);
+               });
         }
       }
     }
+    flush();
     if (lane == 0) {
       __threadfence_block();
       if (!stop) *total_tiles = tiles;
@@ -248,10 +332,10 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
       const int pub = *published;
       __threadfence_block();  // descriptors of chunks < pub are visible
       if (pub > 0) {
-        const ChunkDesc& last = desc[(pub - 1) % M];
-        if (t < last.tile_base + last.ntiles) {
+        const ChunkDesc* last = desc_at((pub - 1) % M);
+        if (t < last->tile_base + last->ntiles) {
           c = pub - 1;
-          while (desc[c % M].tile_base > t) --c;  // within the last M chunks
+          while (desc_at(c % M)->tile_base > t) --c;  // within the last M chunks
           break;
         }
       }
@@ -268,21 +352,32 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
     if (!mbar_wait(full0 + 8u * slot, (c / M) & 1, abort_flag, P.err, P.wait_timeout_ns,
                    kSiteConsumerFull))
       break;
-    const ChunkDesc d = desc[slot];
-    const int nu = 16 / d.smax;
-    const int hl0 = (t - d.tile_base) * nu;
-    const uint32_t cbase = ring0 + d.off;
-    switch (d.smax) {
-      case 1: chunk_tile<D, 1, G>(P, d, hl0, cbase, sc, lane); break;
-      case 2: chunk_tile<D, 2, G>(P, d, hl0, cbase, sc, lane); break;
-      case 4: chunk_tile<D, 4, G>(P, d, hl0, cbase, sc, lane); break;
-      case 8: chunk_tile<D, 8, G>(P, d, hl0, cbase, sc, lane); break;
-      default: chunk_tile<D, 16, G>(P, d, hl0, cbase, sc, lane); break;
+    const ChunkDesc* d = desc_at(slot);
+    const int local = t - d->tile_base;
+    int j = d->nrows - 1;
+    while (j > 0 && d->tstart[j] > local) --j;
+    TileRef ref;
+    ref.b = d->b0 + j;
+    ref.s_len = d->s_len[j];
+    ref.h0 = d->h0;
+    ref.nh = d->nh;
+    ref.koff = d->off + (uint32_t)d->krow[j] * d->nh * (D * 2);
+    ref.voff = ref.koff + d->kv_bytes;
+    ref.qoff = d->off + 2 * d->kv_bytes + (uint32_t)(j * d->nh * G) * (D * 2);
+    const int ntiles = d->ntiles;
+    const int smax = smax_of(ref.s_len);
+    const int hl0 = (local - d->tstart[j]) * (16 / smax);
+    switch (smax) {
+      case 1: chunk_tile<D, 1, G>(P, ref, hl0, ring0, R, sc, lane); break;
+      case 2: chunk_tile<D, 2, G>(P, ref, hl0, ring0, R, sc, lane); break;
+      case 4: chunk_tile<D, 4, G>(P, ref, hl0, ring0, R, sc, lane); break;
+      case 8: chunk_tile<D, 8, G>(P, ref, hl0, ring0, R, sc, lane); break;
+      default: chunk_tile<D, 16, G>(P, ref, hl0, ring0, R, sc, lane); break;
     }
     __syncwarp();
     if (lane == 0) {
       // The chunk's last tile resets the slot's counter and frees the chunk.
-      if (atomicAdd(done + slot, 1) == d.ntiles - 1) {
+      if (atomicAdd(done + slot, 1) == ntiles - 1) {
         done[slot] = 0;
         __threadfence_block();
         mbar_arrive(empty0 + 8u * slot);

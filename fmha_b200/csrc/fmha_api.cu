@@ -398,7 +398,9 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
     if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
     P.sc_off = kVarlenChunkHdr;
     P.ring_off = (P.sc_off + (uint32_t)ncw * g * 16 * 4 + 1023u) & ~1023u;
-    const uint32_t ring = (uint32_t)(dev.smem_optin - (int64_t)P.ring_off) & ~127u;
+    // A multiple of the row size (D*2 bytes, itself a multiple of 128).
+    const uint32_t row_b = (uint32_t)head_dim * 2;
+    const uint32_t ring = (uint32_t)((dev.smem_optin - (int64_t)P.ring_off) / row_b) * row_b;
     P.stage_bytes = ring;
     uint32_t cmax = (uint32_t)env_int("FMHA_VARLEN_CHUNK", 96 * 1024);
     if (cmax > ring / 2) cmax = ring / 2;
