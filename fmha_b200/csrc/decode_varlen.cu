@@ -81,30 +81,40 @@ __global__ void __launch_bounds__(kLdgThreads) decode_varlen_kernel(const Varlen
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   float* sc = sc_all[warp];
-  // Warps take whole batch rows round-robin and walk only the row's real
-  // tiles; the next row's cu_seqlens pair is loaded while this row runs.
+  // Warps take work items round-robin: item = (batch row, head range of hpi
+  // heads, ~4 by default).
+  // A long row (one head per tile) is thereby spread over several warps
+  // instead of landing on one. The next item's cu_seqlens pair is loaded
+  // while this one runs.
+  const int hkv = P.num_heads_kv;
+  const int qs = P.tiles_per_row;  // head ranges per row
+  const int hpi = (hkv + qs - 1) / qs;
+  const int64_t items = P.batch * qs;
   const int64_t stride = (int64_t)gridDim.x * WPB;
-  int64_t b = (int64_t)blockIdx.x * WPB + warp;
+  int64_t it = (int64_t)blockIdx.x * WPB + warp;
   int c0n = 0, c1n = 0;
-  if (b < P.batch) {
-    c0n = __ldg(P.cu_seqlens + b);
-    c1n = __ldg(P.cu_seqlens + b + 1);
+  if (it < items) {
+    c0n = __ldg(P.cu_seqlens + it / qs);
+    c1n = __ldg(P.cu_seqlens + it / qs + 1);
   }
-  for (; b < P.batch; b += stride) {
+  for (; it < items; it += stride) {
+    const int64_t b = it / qs;
+    const int q = (int)(it - b * qs);
     const int c0 = c0n;
     const int s_len = c1n - c0;
-    if (b + stride < P.batch) {
-      c0n = __ldg(P.cu_seqlens + b + stride);
-      c1n = __ldg(P.cu_seqlens + b + stride + 1);
+    if (it + stride < items) {
+      c0n = __ldg(P.cu_seqlens + (it + stride) / qs);
+      c1n = __ldg(P.cu_seqlens + (it + stride) / qs + 1);
     }
     if (s_len < 0 || s_len > P.max_seqlen) {
-      if (lane == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
+      if (lane == 0 && q == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
       continue;
     }
     const int smax = s_len <= 1 ? 1 : s_len <= 2 ? 2 : s_len <= 4 ? 4 : s_len <= 8 ? 8 : 16;
     const int nu = 16 / smax;
-    for (int h0 = 0; h0 < P.num_heads_kv; h0 += nu) {
-      const int nv = P.num_heads_kv - h0 < nu ? P.num_heads_kv - h0 : nu;
+    const int hend = (q + 1) * hpi < hkv ? (q + 1) * hpi : hkv;
+    for (int h0 = q * hpi; h0 < hend; h0 += nu) {
+      const int nv = hend - h0 < nu ? hend - h0 : nu;
       switch (smax) {
         case 1: varlen_tile<D, 1, G>(P, b, c0, s_len, h0, nv, sc, lane); break;
         case 2: varlen_tile<D, 2, G>(P, b, c0, s_len, h0, nv, sc, lane); break;

@@ -377,19 +377,29 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   // FMHA_VARLEN_KERNEL=ldg selects the register-prefetch kernel, =ring the
   // gather ring; the default is the chunk ring.
+  // Default per head_dim (measured on the reference's Poisson(4) table):
+  // D=256 -> the register-prefetch kernel with 4-head work items (16 KB tiles
+  // leave the shared-memory ring too few in flight); D=128 -> the chunk ring.
   static const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
-  if (kind && std::strcmp(kind, "ldg") == 0) {
+  const bool use_ldg = kind ? std::strcmp(kind, "ldg") == 0 : head_dim == 256;
+  if (use_ldg) {
     int bps = 1;
     st = blocks_per_sm(reinterpret_cast<KernelFn>(fn), kLdgThreads, &bps);
     if (st != FMHA_OK) return st;
+    // Head ranges of ~4 heads per work item (FMHA_VARLEN_SPLIT overrides).
+    int qs = num_heads_kv / 4 > 1 ? num_heads_kv / 4 : 1;
+    qs = env_int("FMHA_VARLEN_SPLIT", qs);
+    if (qs < 1) qs = 1;
+    if (qs > num_heads_kv) qs = num_heads_kv;
+    P.tiles_per_row = qs;
     int64_t grid = (int64_t)dev.sms * bps;
-    const int64_t need = ((int64_t)batch + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
+    const int64_t need = ((int64_t)batch * qs + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
     if (grid > need) grid = need;
     fn<<<(unsigned)grid, kLdgThreads, 0, cs>>>(P);
     return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
   }
   if (!(kind && std::strcmp(kind, "ring") == 0)) {
-    // Default: whole packed rows (or head groups) as chunks of a byte ring.
+    // Chunk ring: whole packed rows (or head groups) as chunks of a byte ring.
     VarlenFn cfn = head_dim == 128 ? varlen_chunk_kernel_d128(g) : varlen_chunk_kernel_d256(g);
     if (!cfn) return FMHA_ERR_UNSUPPORTED;
     P.wait_timeout_ns = kWaitTimeoutNs;
