@@ -48,6 +48,7 @@ for _s in (1, 2, 4, 8, 16):
         for _h in (16, 32):
             CONFIGS.setdefault(f"h{_h}_d{_d}_s{_s}", (30720, _h, _h, _s, _d))
     CONFIGS.setdefault(f"gqa_32_16_d256_s{_s}", (30720, 32, 16, _s, 256))
+    CONFIGS.setdefault(f"gqa_32_16_d128_s{_s}", (30720, 32, 16, _s, 128))
     for _hkv in (8, 4):  # 4 and 8 query heads per kv head
         for _d in (128, 256):
             CONFIGS.setdefault(f"gqa_32_{_hkv}_d{_d}_s{_s}", (30720, 32, _hkv, _s, _d))

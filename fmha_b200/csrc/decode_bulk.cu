@@ -124,7 +124,22 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const P
 #pragma unroll
         for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
       };
-      attend_tile16<D, SMAX, G>(loadK, loadV, loadQ, store, s_len, uv, P.scale_log2, sc, lane);
+      if constexpr (G >= kMmaMinHeads && SMAX == 16) {
+        // Four or more query heads per unit of 9..16 rows: tensor-core tile
+        // (rows past s_len, including the next unit's, are masked). Measured:
+        // G=8 S=16 3.2 -> 6.7-6.9 TB/s (D=256); for G=2 or 8-row units the
+        // fp32 CUDA-core tile is faster.
+#pragma unroll
+        for (int u = 0; u < T::NU; ++u) {
+          if (u >= uv) break;
+          const int ju = j * T::NU + u;
+          const uint32_t k0 = sbase + (uint32_t)(ju * s_len) * (D * 2);
+          attend_unit_mma<D, G>(k0, k0 + P.v_off, sbase + P.q_off + (uint32_t)ju * (G * D * 2),
+                                s_len, P.scale_log2, P.O + (tile_u0 + u) * (G * D), lane);
+        }
+      } else {
+        attend_tile16<D, SMAX, G>(loadK, loadV, loadQ, store, s_len, uv, P.scale_log2, sc, lane);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8u * st);  // stage's shared reads are done

@@ -18,6 +18,7 @@
 // touches belongs to the same unit.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -512,6 +513,122 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
         for (int c = 0; c < 8; ++c) acc[g][c] += __shfl_xor_sync(kFullMask, acc[g][c], 16);
     }
     if (!T::CROSS || r0 == 0) store(slot_unit(us), acc);
+  }
+}
+
+// ----------------------------------------------------------------------
+// Tensor-core tile for one unit with several query heads (G = 4 or 8) and up
+// to 16 K/V rows, on mma.sync.m16n8k16 (bf16 operands, fp32 accumulation).
+// With G heads per kv head the fp32 CUDA-core path spends ~G x 16 x 16 FMAs per
+// lane per tile; here the G query rows are the MMA's M rows (rows >= G are
+// zero).
+//  * S = Q K^T: lane (g = lane/4, t = lane%4) loads 16 contiguous bytes of Q
+//    row g and of K rows g and g+8 at column 32j + 8t. The dot product's d
+//    order is free, so those 8 columns become this lane's k slots of two
+//    k-steps (the same rule in A and B keeps every product paired).
+//  * softmax on the accumulators (row g; scores s = 2t, 2t+1, 8+2t, 9+2t),
+//    reduced over the 4 lanes of a row; rows >= s_len are -inf.
+//  * O = P V: the score accumulators are already in A-fragment order. P is
+//    split into bf16 hi + lo (two MMAs) so it keeps ~16 more bits than bf16
+//    alone -- P never drops to bf16 precision. V rows s = 2t, 2t+1, 2t+8,
+//    2t+9 are loaded 16 bytes at a time at column 8g + 64m and repacked into
+//    B fragments; output column n of n-tile (m, i) is then 8n + 64m + i, so
+//    each lane ends with 16 contiguous outputs per m of its head.
+// Rows past s_len are zeroed in V (garbage there must not meet P = 0).
+// Query heads per kv head from which the bulk kernel uses the tensor-core tile
+// (for units of 9..16 rows).
+#ifndef FMHA_MMA_MIN_HEADS
+#define FMHA_MMA_MIN_HEADS 4
+#endif
+constexpr int kMmaMinHeads = FMHA_MMA_MIN_HEADS;
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t half16(const uint4 v, int i) {  // element i of 8
+  const uint32_t w = i < 2 ? v.x : i < 4 ? v.y : i < 6 ? v.z : v.w;
+  return (i & 1) ? (w >> 16) : (w & 0xffffu);
+}
+
+template <int D, int G>
+__device__ __forceinline__ void attend_unit_mma(uint32_t kbase, uint32_t vbase, uint32_t qbase,
+                                                int s_len, float scale_log2, uint16_t* O,
+                                                int lane) {
+  static_assert(G <= 8, "query heads fill at most 8 of the 16 MMA rows");
+  const int g = lane >> 2, t = lane & 3;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    const uint32_t col = (uint32_t)(32 * j + 8 * t) * 2;
+    const uint4 qa = g < G ? lds128(qbase + (uint32_t)g * (D * 2) + col) : z;
+    const uint4 k0 = lds128(kbase + (uint32_t)g * (D * 2) + col);
+    const uint4 k1 = lds128(kbase + (uint32_t)(g + 8) * (D * 2) + col);
+    mma_16816(c0, qa.x, qa.y, k0.x, k0.y);
+    mma_16816(c1, qa.x, qa.y, k1.x, k1.y);
+    mma_16816(c0, qa.z, qa.w, k0.z, k0.w);
+    mma_16816(c1, qa.z, qa.w, k1.z, k1.w);
+  }
+  // Scores of row g: s = 2t, 2t+1 (c0), 8+2t, 9+2t (c1).
+  float x[4] = {c0[0], c0[1], c1[0], c1[1]};
+  const int sidx[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = sidx[i] < s_len ? x[i] * scale_log2 : -INFINITY;
+  float m = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+  m = fmaxf(m, __shfl_xor_sync(kFullMask, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(kFullMask, m, 2));
+  float e[4], sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    e[i] = s_len == 0 ? 0.0f : exp2f(x[i] - m);
+    sum += e[i];
+  }
+  sum += __shfl_xor_sync(kFullMask, sum, 1);
+  sum += __shfl_xor_sync(kFullMask, sum, 2);
+  float p[4], lo[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = s_len == 0 ? 0.0f : e[i] / sum;
+  const uint32_t ah0 = pack_bf16x2(p[0], p[1]), ah2 = pack_bf16x2(p[2], p[3]);
+  lo[0] = p[0] - __uint_as_float(ah0 << 16);
+  lo[1] = p[1] - __uint_as_float(ah0 & 0xffff0000u);
+  lo[2] = p[2] - __uint_as_float(ah2 << 16);
+  lo[3] = p[3] - __uint_as_float(ah2 & 0xffff0000u);
+  const uint32_t al0 = pack_bf16x2(lo[0], lo[1]), al2 = pack_bf16x2(lo[2], lo[3]);
+
+#pragma unroll
+  for (int mm = 0; mm < D / 64; ++mm) {
+    const uint32_t col = (uint32_t)(8 * g + 64 * mm) * 2;
+    const uint4 v0 = 2 * t < s_len ? lds128(vbase + (uint32_t)(2 * t) * (D * 2) + col) : z;
+    const uint4 v1 = 2 * t + 1 < s_len ? lds128(vbase + (uint32_t)(2 * t + 1) * (D * 2) + col) : z;
+    const uint4 v2 = 2 * t + 8 < s_len ? lds128(vbase + (uint32_t)(2 * t + 8) * (D * 2) + col) : z;
+    const uint4 v3 = 2 * t + 9 < s_len ? lds128(vbase + (uint32_t)(2 * t + 9) * (D * 2) + col) : z;
+    float o0[8], o1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b0 = half16(v0, i) | (half16(v1, i) << 16);
+      const uint32_t b1 = half16(v2, i) | (half16(v3, i) << 16);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_16816(acc, ah0, ah2, b0, b1);
+      mma_16816(acc, al0, al2, b0, b1);
+      o0[i] = acc[0];  // output column 8*(2t) + 64mm + i
+      o1[i] = acc[1];  // output column 8*(2t+1) + 64mm + i
+    }
+    if (g < G) {
+      uint16_t* orow = O + (int64_t)g * D + 16 * t + 64 * mm;
+      stg_stream(orow, pack8_f16(o0));
+      stg_stream(orow + 8, pack8_f16(o1));
+    }
   }
 }
 
