@@ -56,6 +56,7 @@ for _s in (1, 2, 4, 8, 16):
 # The reference's own benchmark table (fmha_host.cpp:511-517): packed varlen
 # K/V with Poisson(4) seqlens in [2, 16] (seed 42) -> fmha_forward_varlen.
 VARLEN = {f"varlen_h{_h}_d{_d}": (30720, _h, _h, 16, _d) for _h in (16, 32) for _d in (128, 256)}
+VARLEN.update({f"varlen_gqa_32_16_d{_d}": (30720, 32, 16, 16, _d) for _d in (128, 256)})
 CONFIGS.update(VARLEN)
 
 L2_BYTES = 126 * 1024 * 1024

@@ -53,7 +53,6 @@ def _objects():
     for src, d in (("decode_bulk.cu", 128), ("decode_bulk.cu", 256),
                    ("decode_ldg.cu", 128), ("decode_ldg.cu", 256),
                    ("decode_varlen.cu", 128), ("decode_varlen.cu", 256),
-                   ("decode_varlen_ring.cu", 128), ("decode_varlen_ring.cu", 256),
                    ("decode_varlen_chunk.cu", 128), ("decode_varlen_chunk.cu", 256)):
         stem = src[:-3]
         objs.append((os.path.join(CSRC, src), os.path.join(BUILD, f"{stem}_d{d}.o"),

@@ -674,26 +674,20 @@ struct VarlenParams {
   int max_seqlen;     // rows longer than this are rejected (device error)
   int tiles_per_row;  // 16-row tiles of a row of length max_seqlen (ldg kernel)
   float scale_log2;   // log2(e) * softmax scale
-  // ring kernel only
+  // chunk kernel only
   unsigned long long wait_timeout_ns;
-  int stages;            // ring stages, one 16-row tile each; a multiple of the consumers
-  uint32_t stage_bytes;  // descriptor + 16 K rows + 16 V rows + 16*G Q rows
+  uint32_t stage_bytes;  // ring size in bytes (a multiple of the row size)
   uint32_t sc_off;       // per-consumer-warp score scratch
-  uint32_t ring_off;     // first stage
-  int producers;         // gathering warps (ring kernel)
-  uint32_t chunk_max;    // chunk kernel: byte limit of one chunk (<= ring/2)
+  uint32_t ring_off;     // first ring byte
+  uint32_t chunk_max;    // byte limit of one chunk (<= ring/2)
 };
 using VarlenFn = void (*)(const VarlenParams);
 VarlenFn varlen_kernel_d128(int g);
 VarlenFn varlen_kernel_d256(int g);
-VarlenFn varlen_ring_kernel_d128(int g);
-VarlenFn varlen_ring_kernel_d256(int g);
 VarlenFn varlen_chunk_kernel_d128(int g);
 VarlenFn varlen_chunk_kernel_d256(int g);
 constexpr int kVarlenSlots = 32;           // chunk descriptors in flight per CTA
 constexpr uint32_t kVarlenChunkHdr = 8192;  // barriers, counters, descriptors
-constexpr uint32_t kVarlenDescBytes = 64;
-constexpr int kVarlenProducers = 6;  // default gathering warps per varlen ring CTA
 
 // Per-head_dim lookups of the instantiation for (SMAX, G); nullptr if absent.
 KernelFn bulk_kernel_d128(int smax, int g);

@@ -375,13 +375,12 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
                                             : 1.0 / std::sqrt((double)head_dim);
   P.scale_log2 = (float)(1.4426950408889634 * scale);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  // FMHA_VARLEN_KERNEL=ldg selects the register-prefetch kernel, =ring the
-  // gather ring; the default is the chunk ring.
+  // FMHA_VARLEN_KERNEL=ldg|chunk overrides the per-head_dim default below.
   // Default per head_dim (measured on the reference's Poisson(4) table):
   // D=256 -> the register-prefetch kernel with 4-head work items (16 KB tiles
   // leave the shared-memory ring too few in flight); D=128 -> the chunk ring.
   static const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
-  const bool use_ldg = kind ? std::strcmp(kind, "ldg") == 0 : head_dim == 256;
+  const bool use_ldg = (kind && *kind) ? std::strcmp(kind, "ldg") == 0 : head_dim == 256;
   if (use_ldg) {
     int bps = 1;
     st = blocks_per_sm(reinterpret_cast<KernelFn>(fn), kLdgThreads, &bps);
@@ -398,75 +397,29 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
     fn<<<(unsigned)grid, kLdgThreads, 0, cs>>>(P);
     return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
   }
-  if (!(kind && std::strcmp(kind, "ring") == 0)) {
-    // Chunk ring: whole packed rows (or head groups) as chunks of a byte ring.
-    VarlenFn cfn = head_dim == 128 ? varlen_chunk_kernel_d128(g) : varlen_chunk_kernel_d256(g);
-    if (!cfn) return FMHA_ERR_UNSUPPORTED;
-    P.wait_timeout_ns = kWaitTimeoutNs;
-    int ncw = env_int("FMHA_VARLEN_WARPS", 16);
-    if (ncw < 1) ncw = 1;
-    if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
-    P.sc_off = kVarlenChunkHdr;
-    P.ring_off = (P.sc_off + (uint32_t)ncw * g * 16 * 4 + 1023u) & ~1023u;
-    // A multiple of the row size (D*2 bytes, itself a multiple of 128).
-    const uint32_t row_b = (uint32_t)head_dim * 2;
-    const uint32_t ring = (uint32_t)((dev.smem_optin - (int64_t)P.ring_off) / row_b) * row_b;
-    P.stage_bytes = ring;
-    uint32_t cmax = (uint32_t)env_int("FMHA_VARLEN_CHUNK", 96 * 1024);
-    if (cmax > ring / 2) cmax = ring / 2;
-    // One head of the longest row must fit in a chunk.
-    const uint32_t one = (uint32_t)(2 * max_seqlen_kv + g) * head_dim * 2;
-    if (one > cmax) return FMHA_ERR_UNSUPPORTED;
-    P.chunk_max = cmax;
-    st = ensure_smem(reinterpret_cast<KernelFn>(cfn), dev.smem_optin);
-    if (st != FMHA_OK) return st;
-    const int grid = batch < dev.sms ? batch : dev.sms;
-    cfn<<<grid, 32 * (1 + ncw), P.ring_off + ring, cs>>>(P);
-    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
-  }
-  VarlenFn rfn = head_dim == 128 ? varlen_ring_kernel_d128(g) : varlen_ring_kernel_d256(g);
-  if (!rfn) return FMHA_ERR_UNSUPPORTED;
+  // Chunk ring: whole packed rows (or head groups) as chunks of a byte ring.
+  VarlenFn cfn = head_dim == 128 ? varlen_chunk_kernel_d128(g) : varlen_chunk_kernel_d256(g);
+  if (!cfn) return FMHA_ERR_UNSUPPORTED;
   P.wait_timeout_ns = kWaitTimeoutNs;
-  int npw = env_int("FMHA_VARLEN_PRODUCERS", kVarlenProducers);  // measured best: 6
-  if (npw < 1) npw = 1;
-  if (npw > 8) npw = 8;
-  P.producers = npw;
-  int ncw = env_int("FMHA_VARLEN_WARPS", 8);
+  int ncw = env_int("FMHA_VARLEN_WARPS", 16);
   if (ncw < 1) ncw = 1;
-  if (ncw > kBulkMaxThreads / 32 - npw) ncw = kBulkMaxThreads / 32 - npw;
-  const uint32_t stage =
-      (kVarlenDescBytes + 32u * head_dim * 2 + 16u * g * head_dim * 2 + 127u) & ~127u;
-  P.sc_off = kHdrBytes;
+  if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
+  P.sc_off = kVarlenChunkHdr;
   P.ring_off = (P.sc_off + (uint32_t)ncw * g * 16 * 4 + 1023u) & ~1023u;
-  int ns = (int)((dev.smem_optin - (int64_t)P.ring_off) / stage);
-  const int ns_cap = env_int("FMHA_STAGES", kMaxStages);
-  if (ns > ns_cap) ns = ns_cap;
-  if (ns > kMaxStages) ns = kMaxStages;
-  // Producer and consumer warps both own whole stages: the stage count is a
-  // multiple of both warp counts, so stage st's phases are armed by one
-  // producer and consumed by one consumer, each in order, and no parity wait
-  // can refer to a phase two behind (try_wait.parity would call that one
-  // complete).
-  auto lcm = [](int a, int b) {
-    int x = a, y = b;
-    while (y) { const int t = x % y; x = y; y = t; }
-    return a / x * b;
-  };
-  while (lcm(npw, ncw) > ns && (ncw > 1 || npw > 1)) {
-    if (ncw > 1) --ncw;
-    else --npw;
-  }
-  P.producers = npw;
-  const int unit = lcm(npw, ncw);
-  if (unit > ns) return FMHA_ERR_UNSUPPORTED;
-  ns -= ns % unit;
-  P.stages = ns;
-  P.stage_bytes = stage;
-  const uint32_t smem = P.ring_off + (uint32_t)ns * stage;
-  st = ensure_smem(reinterpret_cast<KernelFn>(rfn), dev.smem_optin);
+  // A multiple of the row size (D*2 bytes, itself a multiple of 128).
+  const uint32_t row_b = (uint32_t)head_dim * 2;
+  const uint32_t ring = (uint32_t)((dev.smem_optin - (int64_t)P.ring_off) / row_b) * row_b;
+  P.stage_bytes = ring;
+  uint32_t cmax = (uint32_t)env_int("FMHA_VARLEN_CHUNK", 96 * 1024);
+  if (cmax > ring / 2) cmax = ring / 2;
+  // One head of the longest row must fit in a chunk.
+  const uint32_t one = (uint32_t)(2 * max_seqlen_kv + g) * head_dim * 2;
+  if (one > cmax) return FMHA_ERR_UNSUPPORTED;
+  P.chunk_max = cmax;
+  st = ensure_smem(reinterpret_cast<KernelFn>(cfn), dev.smem_optin);
   if (st != FMHA_OK) return st;
   const int grid = batch < dev.sms ? batch : dev.sms;
-  rfn<<<grid, 32 * (npw + ncw), smem, cs>>>(P);
+  cfn<<<grid, 32 * (1 + ncw), P.ring_off + ring, cs>>>(P);
   return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
 }
 

@@ -75,6 +75,10 @@ def _fault_worker(rank, world, port, outdir, mode):
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
                           timeout=datetime.timedelta(seconds=20))
     mon = ShardMonitor(store, rank, world, prefix=f"t-{mode}")
+    # Start-up handshake: process spawn and imports can skew ranks by seconds,
+    # which is not the fault under test.
+    mon.report(-1, ok=True)
+    assert mon.wait_step(-1, timeout_s=60.0) == ({}, [])
     log = []
     for step in range(3):
         if rank == 1 and step == 1:
