@@ -69,26 +69,26 @@ fmha_status_t device_info(DeviceInfo* out) {
 }
 
 // Sets the kernel's dynamic shared-memory limit once per (kernel, device).
-fmha_status_t ensure_smem(KernelFn fn, int bytes) {
+fmha_status_t ensure_smem(const void* fn, int bytes) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_mu);
-  auto key = std::make_pair(reinterpret_cast<const void*>(fn), dev);
+  auto key = std::make_pair(fn, dev);
   if (g_smem_set.count(key)) return FMHA_OK;
   // The limit is set to the device maximum, so one call covers every plan.
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
     return FMHA_ERR_CUDA;
   g_smem_set.insert(key);
   return FMHA_OK;
 }
 
-fmha_status_t blocks_per_sm(KernelFn fn, int threads, int* out) {
+fmha_status_t blocks_per_sm(const void* fn, int threads, int* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_mu);
   for (int i = 0; i < g_occ_n; ++i)
-    if (g_occ[i].fn == reinterpret_cast<const void*>(fn) && g_occ[i].dev == dev) {
+    if (g_occ[i].fn == fn && g_occ[i].dev == dev) {
       *out = g_occ[i].blocks;
       return FMHA_OK;
     }
@@ -96,7 +96,7 @@ fmha_status_t blocks_per_sm(KernelFn fn, int threads, int* out) {
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fn, threads, 0) != cudaSuccess)
     return FMHA_ERR_CUDA;
   if (b < 1) b = 1;
-  if (g_occ_n < 512) g_occ[g_occ_n++] = {reinterpret_cast<const void*>(fn), dev, b};
+  if (g_occ_n < 512) g_occ[g_occ_n++] = {fn, dev, b};
   *out = b;
   return FMHA_OK;
 }
@@ -204,7 +204,7 @@ fmha_status_t launch_bulk(Params P, int d, int smax, int g, int warps, const Dev
   P.q_off = 2 * kb;
   P.sc_off = sc_off;
   P.ring_off = ring_off;
-  fmha_status_t st = ensure_smem(fn, dev.smem_optin);
+  fmha_status_t st = ensure_smem(reinterpret_cast<const void*>(fn), dev.smem_optin);
   if (st != FMHA_OK) return st;
   int grid = dev.sms * ctas_per_sm;
   if (grid > P.chunks) grid = P.chunks;
@@ -244,7 +244,7 @@ fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev
   const int64_t tiles = (P.units + nu - 1) / nu;
   const int wpb = kLdgThreads / 32;
   int bps = 1;
-  fmha_status_t st = blocks_per_sm(fn, kLdgThreads, &bps);
+  fmha_status_t st = blocks_per_sm(reinterpret_cast<const void*>(fn), kLdgThreads, &bps);
   if (st != FMHA_OK) return st;
   const int64_t need = (tiles + (int64_t)wpb * tpi - 1) / ((int64_t)wpb * tpi);
   int64_t grid = (int64_t)dev.sms * bps;
@@ -383,7 +383,7 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
   const bool use_ldg = (kind && *kind) ? std::strcmp(kind, "ldg") == 0 : head_dim == 256;
   if (use_ldg) {
     int bps = 1;
-    st = blocks_per_sm(reinterpret_cast<KernelFn>(fn), kLdgThreads, &bps);
+    st = blocks_per_sm(reinterpret_cast<const void*>(fn), kLdgThreads, &bps);
     if (st != FMHA_OK) return st;
     // Head ranges of ~4 heads per work item (FMHA_VARLEN_SPLIT overrides).
     int qs = num_heads_kv / 4 > 1 ? num_heads_kv / 4 : 1;
@@ -416,7 +416,7 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
   const uint32_t one = (uint32_t)(2 * max_seqlen_kv + g) * head_dim * 2;
   if (one > cmax) return FMHA_ERR_UNSUPPORTED;
   P.chunk_max = cmax;
-  st = ensure_smem(reinterpret_cast<KernelFn>(cfn), dev.smem_optin);
+  st = ensure_smem(reinterpret_cast<const void*>(cfn), dev.smem_optin);
   if (st != FMHA_OK) return st;
   const int grid = batch < dev.sms ? batch : dev.sms;
   cfn<<<grid, 32 * (1 + ncw), P.ring_off + ring, cs>>>(P);
