@@ -175,6 +175,8 @@ void cpu_row(const uint16_t* q, const uint16_t* k, const uint16_t* v, int hq, in
 
 // ------------------------------------------------------------ per-GPU shard
 
+// Start line for the timed loops. A shard that fails before it gets there
+// drops out (drop()), so the others are not left waiting for it.
 struct HostBarrier {
   std::mutex mu;
   std::condition_variable cv;
@@ -182,7 +184,7 @@ struct HostBarrier {
   void wait() {
     std::unique_lock<std::mutex> lk(mu);
     const int g = gen;
-    if (++count == n) {
+    if (++count >= n) {
       count = 0;
       ++gen;
       cv.notify_all();
@@ -190,9 +192,19 @@ struct HostBarrier {
       cv.wait(lk, [&] { return gen != g; });
     }
   }
+  void drop() {
+    std::unique_lock<std::mutex> lk(mu);
+    --n;
+    if (count >= n && count > 0) {
+      count = 0;
+      ++gen;
+      cv.notify_all();
+    }
+  }
 };
 
 struct ShardResult {
+  std::string error;  // empty when the shard completed
   double ms_per_iter = 0;
   int64_t rows_checked = 0;
   int64_t bad = 0;
@@ -201,59 +213,124 @@ struct ShardResult {
   int device_error = 0;
 };
 
+// Shard-local error handling: record the failure and leave the shard (the
+// other shards keep running and the driver reports every failed shard).
+#define SHARD_CUDA(cmd)                                                                      \
+  do {                                                                                       \
+    cudaError_t e_ = (cmd);                                                                  \
+    if (e_ != cudaSuccess) {                                                                 \
+      res.error = std::string(#cmd) + ": " + cudaGetErrorString(e_);                         \
+      cleanup();                                                                             \
+      return;                                                                                \
+    }                                                                                        \
+  } while (0)
+#define SHARD_FMHA(cmd)                                                                      \
+  do {                                                                                       \
+    fmha_status_t s_ = (cmd);                                                                \
+    if (s_ != FMHA_OK) {                                                                     \
+      res.error = std::string(#cmd) + ": " + fmha_status_string(s_);                         \
+      cleanup();                                                                             \
+      return;                                                                                \
+    }                                                                                        \
+  } while (0)
+
+// Waits for an event by polling with a deadline instead of blocking forever.
+bool wait_event(cudaEvent_t e, double timeout_s, std::string* why) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(e);
+    if (q == cudaSuccess) return true;
+    if (q != cudaErrorNotReady) {
+      *why = std::string("cudaEventQuery: ") + cudaGetErrorString(q);
+      return false;
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+      *why = "timed out waiting for the shard's kernels";
+      return false;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+int injected_failure_shard() {
+  const char* v = std::getenv("FMHA_HOST_FAIL_SHARD");
+  return (v && *v) ? std::atoi(v) : -1;
+}
+
 // cu: global cu_seqlens (varlen mode) or empty.
 void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64_t rows,
                const std::vector<int64_t>& cu, HostBarrier& bar, ShardResult& res) {
-  CUDA_CHECK(cudaSetDevice(gpu));
   const int hq = cfg.num_heads_q, hkv = cfg.num_heads_kv, d = cfg.head_dim, s = o.seqlen;
   const bool vl = o.varlen;
   const int64_t t0row = vl ? cu[row0] : row0 * s;  // first K/V row (packed) of the shard
   const int64_t nq = rows * hq * d;
   const int64_t nkv = vl ? (cu[row0 + rows] - cu[row0]) * hkv * d : rows * hkv * s * d;
-  void *dQ, *dK, *dV, *dO, *dCu = nullptr;
-  CUDA_CHECK(cudaMalloc(&dQ, nq * 2));
-  CUDA_CHECK(cudaMalloc(&dK, nkv * 2));
-  CUDA_CHECK(cudaMalloc(&dV, nkv * 2));
-  CUDA_CHECK(cudaMalloc(&dO, nq * 2));
-  cudaStream_t st;
-  CUDA_CHECK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  void *dQ = nullptr, *dK = nullptr, *dV = nullptr, *dO = nullptr, *dCu = nullptr;
+  cudaStream_t st = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  bool started = false;  // passed the start line
+  auto cleanup = [&] {
+    if (!started) bar.drop();
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dQ);
+    cudaFree(dK);
+    cudaFree(dV);
+    cudaFree(dO);
+    if (dCu) cudaFree(dCu);
+  };
+  if (gpu == injected_failure_shard()) {  // host-side fault injection (no GPU fault)
+    res.error = "injected failure (FMHA_HOST_FAIL_SHARD)";
+    cleanup();
+    return;
+  }
+  SHARD_CUDA(cudaSetDevice(gpu));
+  SHARD_CUDA(cudaMalloc(&dQ, nq * 2));
+  SHARD_CUDA(cudaMalloc(&dK, nkv * 2));
+  SHARD_CUDA(cudaMalloc(&dV, nkv * 2));
+  SHARD_CUDA(cudaMalloc(&dO, nq * 2));
+  SHARD_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
   fmha_stream_t fs = reinterpret_cast<fmha_stream_t>(st);
-  FMHA_CHECK(fmha_fill_normal_bf16(dQ, nq, o.seed, 1, row0 * hq * d, fs));
-  FMHA_CHECK(fmha_fill_normal_bf16(dK, nkv, o.seed, 2, t0row * hkv * d, fs));
-  FMHA_CHECK(fmha_fill_normal_bf16(dV, nkv, o.seed, 3, t0row * hkv * d, fs));
-  CUDA_CHECK(cudaMemsetAsync(dO, 0, nq * 2, st));
+  SHARD_FMHA(fmha_fill_normal_bf16(dQ, nq, o.seed, 1, row0 * hq * d, fs));
+  SHARD_FMHA(fmha_fill_normal_bf16(dK, nkv, o.seed, 2, t0row * hkv * d, fs));
+  SHARD_FMHA(fmha_fill_normal_bf16(dV, nkv, o.seed, 3, t0row * hkv * d, fs));
+  SHARD_CUDA(cudaMemsetAsync(dO, 0, nq * 2, st));
   if (vl) {
     std::vector<int32_t> lcu(rows + 1);
     for (int64_t r = 0; r <= rows; ++r) lcu[r] = (int32_t)(cu[row0 + r] - cu[row0]);
-    CUDA_CHECK(cudaMalloc(&dCu, (rows + 1) * 4));
-    CUDA_CHECK(cudaMemcpy(dCu, lcu.data(), (rows + 1) * 4, cudaMemcpyHostToDevice));
+    SHARD_CUDA(cudaMalloc(&dCu, (rows + 1) * 4));
+    SHARD_CUDA(cudaMemcpy(dCu, lcu.data(), (rows + 1) * 4, cudaMemcpyHostToDevice));
   }
   auto launch = [&] {
     if (vl) {
-      FMHA_CHECK(fmha_forward_varlen(dQ, dK, dV, dO, static_cast<const int32_t*>(dCu), (int)rows,
+      SHARD_FMHA(fmha_forward_varlen(dQ, dK, dV, dO, static_cast<const int32_t*>(dCu), (int)rows,
                                      hq, hkv, 16, d, 0.0f, fs));
     } else {
-      FMHA_CHECK(fmha_forward_variant(dQ, dK, dV, dO, (int)rows, hq, hkv, s, d, o.variant, fs));
+      SHARD_FMHA(fmha_forward_variant(dQ, dK, dV, dO, (int)rows, hq, hkv, s, d, o.variant, fs));
     }
   };
   for (int i = 0; i < o.warmups; ++i) launch();
-  CUDA_CHECK(cudaStreamSynchronize(st));
-  cudaEvent_t e0, e1;
-  CUDA_CHECK(cudaEventCreate(&e0));
-  CUDA_CHECK(cudaEventCreate(&e1));
+  SHARD_CUDA(cudaStreamSynchronize(st));
+  SHARD_CUDA(cudaEventCreate(&e0));
+  SHARD_CUDA(cudaEventCreate(&e1));
   bar.wait();  // every GPU starts its timed loop together
-  CUDA_CHECK(cudaEventRecord(e0, st));
+  started = true;
+  SHARD_CUDA(cudaEventRecord(e0, st));
   for (int i = 0; i < o.iters; ++i) launch();
-  CUDA_CHECK(cudaEventRecord(e1, st));
-  CUDA_CHECK(cudaEventSynchronize(e1));
+  SHARD_CUDA(cudaEventRecord(e1, st));
+  if (!wait_event(e1, 120.0, &res.error)) {
+    cleanup();
+    return;
+  }
   float ms = 0;
-  CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+  SHARD_CUDA(cudaEventElapsedTime(&ms, e0, e1));
   res.ms_per_iter = ms / o.iters;
-  FMHA_CHECK(fmha_device_error(&res.device_error));
+  SHARD_FMHA(fmha_device_error(&res.device_error));
 
   // Validation: a deterministic sample of this shard's rows (all if few).
   std::vector<uint16_t> hO(nq);
-  CUDA_CHECK(cudaMemcpy(hO.data(), dO, nq * 2, cudaMemcpyDeviceToHost));
+  SHARD_CUDA(cudaMemcpy(hO.data(), dO, nq * 2, cudaMemcpyDeviceToHost));
   std::vector<int64_t> pick;
   if (o.validate_rows <= 0 || rows <= o.validate_rows) {
     for (int64_t r = 0; r < rows; ++r) pick.push_back(r);
@@ -294,14 +371,7 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
   res.bad = bad;
   res.max_abs = max_abs;
   res.max_rel = max_rel;
-  cudaEventDestroy(e0);
-  cudaEventDestroy(e1);
-  cudaStreamDestroy(st);
-  cudaFree(dQ);
-  cudaFree(dK);
-  cudaFree(dV);
-  cudaFree(dO);
-  if (dCu) cudaFree(dCu);
+  cleanup();
 }
 
 bool run_config(int idx, const Options& o) {
@@ -333,7 +403,18 @@ bool run_config(int idx, const Options& o) {
   double ms = 0, cpu_sec = 0, max_abs = 0, max_rel = 0;
   int64_t bad = 0, checked = 0;
   int dev_err = 0;
+  std::string failed;  // "gpu: reason; ..." for every shard that did not complete
+  double done_frac = 0.0;  // share of the batch whose shard completed
+  for (int g = 0; g < n; ++g) {
+    if (res[g].error.empty()) {
+      done_frac += (double)((int64_t)cfg.batch * (g + 1) / n - (int64_t)cfg.batch * g / n) / cfg.batch;
+      continue;
+    }
+    failed += (failed.empty() ? "" : "; ") + std::to_string(g) + ": " + res[g].error;
+    std::fprintf(stderr, "shard on GPU %d failed: %s\n", g, res[g].error.c_str());
+  }
   for (auto& r : res) {
+    if (!r.error.empty()) continue;
     ms = std::max(ms, r.ms_per_iter);
     bad += r.bad;
     checked += r.rows_checked;
@@ -345,23 +426,26 @@ bool run_config(int idx, const Options& o) {
   const double b = cfg.batch;
   // Byte and flop formulas of fmha_host.cpp:413-414,428-431.
   const double T = (double)total_rows;
-  const double bytes = 2.0 * b * hq * d + 4.0 * T * hkv * d + 2.0 * b * hq * d;
-  const double flops = 4.0 * hq * T * d;
-  const double gbs = bytes / (ms * 1e-3) / 1e9;
+  // Bytes and flops of the completed shards (all of them when none failed).
+  const double bytes = (2.0 * b * hq * d + 4.0 * T * hkv * d + 2.0 * b * hq * d) * done_frac;
+  const double flops = 4.0 * hq * T * d * done_frac;
+  const double gbs = ms > 0 ? bytes / (ms * 1e-3) / 1e9 : 0.0;
   const double cpu_ms_per_row = checked ? cpu_sec * 1e3 / checked * n : 0;  // per-thread-set
   const int threads = omp_get_max_threads();
-  const bool ok = bad == 0 && dev_err == 0;
+  const bool ok = bad == 0 && dev_err == 0 && failed.empty();
+  const bool any = ms > 0;  // at least one shard completed
   if (o.json) {
     std::printf(
         "{\"config\": %d, \"note\": \"%s\", \"batch\": %d, \"num_heads_q\": %d, "
         "\"num_heads_kv\": %d, \"seqlen_kv\": %d, \"head_dim\": %d, \"gpus\": %d, "
         "\"us_per_call\": %.3f, \"gbs\": %.1f, \"tflops\": %.3f, \"rows_checked\": %lld, "
         "\"bad\": %lld, \"max_abs_err\": %.3e, \"max_rel_err\": %.3e, \"cpu_ms_per_row\": %.4f, "
-        "\"cpu_threads\": %d, \"device_error\": %d, \"varlen\": %s, \"passed\": %s}\n",
+        "\"cpu_threads\": %d, \"device_error\": %d, \"varlen\": %s, \"failed_shards\": \"%s\", "
+        "\"passed\": %s}\n",
         idx, cfg.note, cfg.batch, hq, hkv, o.varlen ? -1 : s, d, n, ms * 1e3, gbs,
-        flops / (ms * 1e-3) / 1e12,
+        any ? flops / (ms * 1e-3) / 1e12 : 0.0,
         (long long)checked, (long long)bad, max_abs, max_rel, cpu_ms_per_row, threads, dev_err,
-        o.varlen ? "true" : "false", ok ? "true" : "false");
+        o.varlen ? "true" : "false", failed.c_str(), ok ? "true" : "false");
   } else {
     std::printf("\n=== Configuration %d (%s) ===\n", idx, cfg.note);
     if (o.varlen) {

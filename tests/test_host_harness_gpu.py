@@ -27,3 +27,16 @@ def test_fmha_host_validates(cuda, args):
     assert line["passed"] and line["bad"] == 0 and line["device_error"] == 0
     assert line["us_per_call"] > 0 and line["gbs"] > 0
     assert line["max_abs_err"] <= 2e-3 or line["max_rel_err"] <= 1e-2
+
+
+def test_fmha_host_reports_a_failed_shard(cuda):
+    """Host-side fault injection: the shard on GPU 0 fails before launching
+    anything; the driver reports it (and, with more GPUs, the others still
+    finish) and exits non-zero instead of crashing or hanging."""
+    env = dict(os.environ, FMHA_HOST_FAIL_SHARD="0")
+    r = subprocess.run([BIN, "0", "--json", "--iters", "3"], capture_output=True, text=True,
+                       timeout=300, env=env)
+    assert r.returncode != 0
+    assert "shard on GPU 0 failed: injected failure" in r.stderr
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert not line["passed"] and line["failed_shards"].startswith("0: injected failure")
