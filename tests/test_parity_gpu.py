@@ -180,3 +180,34 @@ def test_full_size_properties(cuda, oracle, hq, hkv, s, d):
         check_close(got, ref32)
     del Q, K, V, O, O2
     cuda.cuda.empty_cache()
+
+
+SWEEP = [(h, h, s, d) for s in (1, 2, 4, 8, 16) for d in (128, 256) for h in (16, 32)] + \
+    [(32, 16, s, 256) for s in (1, 2, 4, 8, 16)]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("hq,hkv,s,d", SWEEP, ids=str)
+def test_full_size_sweep_sampled(cuda, oracle, hq, hkv, s, d):
+    """Every BASELINE sweep shape (S x D x H, plus GQA 32/16 over S) at
+    batch 30720 through fmha_forward (AUTO family): 12 sampled rows, the
+    first and the last, against the oracle at the library tolerance."""
+    B = 30720
+    Q = cuda.empty(B * hq * d, dtype=cuda.bfloat16, device="cuda")
+    K = cuda.empty(B * hkv * s * d, dtype=cuda.bfloat16, device="cuda")
+    V = cuda.empty_like(K)
+    for t, tid in ((Q, 1), (K, 2), (V, 3)):
+        fmha_b200.fill_normal_bf16(t, seed=7, tensor_id=tid)
+    O = cuda.empty(B * hq * d, dtype=cuda.float16, device="cuda")
+    assert fmha_b200.fmha_forward_ptr(Q, K, V, O, B, hq, hkv, s, d) == 0
+    cuda.cuda.synchronize()
+    assert fmha_b200.device_error() == 0
+    rows = np.unique(np.concatenate([np.random.default_rng(s * d + hq).integers(0, B, 10),
+                                     [0, B - 1]]))
+    for b0 in rows:
+        q, k, v = oracle.make_inputs_bhsd(1, hq, hkv, s, d, seed=7, batch_offset=int(b0))
+        ref32, _ = oracle.decode_bhsd(q, k, v, 1, hq, hkv, s, d)
+        got = O[b0 * hq * d:(b0 + 1) * hq * d].cpu().view(cuda.int16).numpy().view(np.uint16)
+        check_close(got, ref32)
+    del Q, K, V, O
+    cuda.cuda.empty_cache()
