@@ -302,6 +302,8 @@ def main():
                     help="comma-separated config names for --sweep (default: all)")
     ap.add_argument("--sweep-warps", default="8,16",
                     help="bulk consumer-warp counts to try in --sweep")
+    ap.add_argument("--sweep-auto", action="store_true",
+                    help="--sweep with the library's own per-shape choice only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -339,6 +341,8 @@ def main():
     if args.sweep:
         names = [x for x in args.sweep_configs.split(",") if x] or sorted(CONFIGS)
         trials = [("ldg", None)] + [("bulk", int(w)) for w in args.sweep_warps.split(",") if w]
+        if args.sweep_auto:
+            trials = [("auto", None)]
         for name in names:
             cfg_n = CONFIGS[name]
             if args.batch > 0:
@@ -347,8 +351,8 @@ def main():
                 if warps is not None:
                     os.environ["FMHA_BULK_WARPS"] = str(warps)
                 if name in VARLEN:
-                    if var != "ldg":
-                        continue  # one varlen family
+                    if var not in ("ldg", "auto"):
+                        continue  # one varlen line
                     r = time_varlen(torch, fmha_b200, cfg_n, world, rank, args, barrier,
                                     max_over_ranks, dev)
                 else:

@@ -124,10 +124,10 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const P
 #pragma unroll
         for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
       };
-      if constexpr (G >= kMmaMinHeads && SMAX == 16) {
-        // Four or more query heads per unit of 9..16 rows: tensor-core tile
-        // (rows past s_len, including the next unit's, are masked). Measured:
-        // G=8 S=16 3.2 -> 6.7-6.9 TB/s (D=256); for G=2 or 8-row units the
+      if constexpr (G >= kMmaMinHeads && SMAX >= 8) {
+        // Four or more query heads per unit of 5..16 rows: tensor-core tile,
+        // one unit at a time (rows past s_len, including the next unit's, are
+        // masked). Measured: G=8 S=16 3.2 -> 6.7-6.9 TB/s (D=256); for G=2 the
         // fp32 CUDA-core tile is faster.
 #pragma unroll
         for (int u = 0; u < T::NU; ++u) {

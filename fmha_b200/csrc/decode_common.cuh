@@ -536,7 +536,7 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
 //    each lane ends with 16 contiguous outputs per m of its head.
 // Rows past s_len are zeroed in V (garbage there must not meet P = 0).
 // Query heads per kv head from which the bulk kernel uses the tensor-core tile
-// (for units of 9..16 rows).
+// (for units of 5..16 rows).
 #ifndef FMHA_MMA_MIN_HEADS
 #define FMHA_MMA_MIN_HEADS 4
 #endif

@@ -132,10 +132,11 @@ Choice auto_choice(int d, int smax, int g) {
   static const int forced = env_int("FMHA_VARIANT", 0);
   Choice c{FMHA_VARIANT_BULK, 16};
   if (g >= 4) {
-    // 4 or 8 query heads per kv head (measured separately).
-    if (d == 128) c = smax <= 2 ? Choice{FMHA_VARIANT_LDG, 0} : Choice{FMHA_VARIANT_BULK, 16};
-    else if (smax >= 8) c = {FMHA_VARIANT_BULK, 10};
-    else if (g == 4 && smax == 1) c = {FMHA_VARIANT_BULK, 10};
+    // 4 or 8 query heads per kv head (measured separately; S >= 5 runs the
+    // bulk kernel's tensor-core tile).
+    if (d == 128) c = smax == 1 ? Choice{FMHA_VARIANT_LDG, 0} : Choice{FMHA_VARIANT_BULK, 16};
+    else if (smax >= 8) c = {FMHA_VARIANT_BULK, 8};
+    else if (g == 4 && smax == 1) c = {FMHA_VARIANT_BULK, 8};
     else c = {FMHA_VARIANT_LDG, 0};
   } else if (d == 256 && smax == 16 && g == 1) c = {FMHA_VARIANT_LDG, 0};
   else if (d == 128 && smax == 1 && g == 1) c = {FMHA_VARIANT_LDG, 0};
