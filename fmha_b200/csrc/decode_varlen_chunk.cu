@@ -14,16 +14,20 @@
 // every chunk large, which is what keeps the bulk copies efficient.
 //
 // Per CTA (persistent, one per SM): a contiguous range of batch rows.
-//  * Producer (warp 0) walks the rows in order (cu_seqlens read 31 rows per
-//    warp load), allocates each chunk in a circular byte ring whose size is a
+//  * Producer (warp 0) plans 32 rows at a time: each lane loads its row's
+//    cu_seqlens pair and sizes the row, then every lane runs the same greedy
+//    packing over the window from shared memory (no shuffle chains), so each
+//    lane knows its row's chunk, index, first K/V row and first tile. Per
+//    chunk it then allocates the chunk in a circular byte ring whose size is a
 //    multiple of one row (D*2 bytes), so a chunk may wrap past the end
 //    without any row straddling it (copies that cross are split in two;
 //    readers wrap their row offsets), and no space is lost to padding; writes
 //    the chunk's
 //    descriptor (per-row lengths, offsets and first tiles) into slot
 //    c % kSlots, arms the slot's `full` mbarrier with the chunk's byte count
-//    and issues the copies: one bulk copy each for K, V and Q of whole rows,
-//    or one K and one V copy per position for a head group.
+//    and issues the copies: one bulk copy each for K, V and Q of whole rows
+//    (lanes 0-2 together), or one K and one V copy per position for a head
+//    group.
 //    It then publishes the chunk count. Ring space and slots are reclaimed in
 //    chunk order by waiting on each slot's `empty` mbarrier, one phase after
 //    another (a single producer walks every slot's phases in order).
@@ -51,6 +55,9 @@ namespace fmha {
 namespace {
 
 constexpr int kChunkRows = 8;  // whole batch rows per chunk at most
+#ifndef FMHA_VARLEN_SPIN_NS
+#define FMHA_VARLEN_SPIN_NS 128
+#endif  // whole batch rows per chunk at most
 
 struct alignas(16) ChunkDesc {
   int64_t b0;         // first batch row
@@ -69,6 +76,12 @@ struct alignas(16) ChunkDesc {
 };
 static_assert(sizeof(ChunkDesc) <= 112, "descriptor size");
 constexpr uint32_t kDescStride = 112;
+// Producer plan arrays (32 rows + 32 entries of int4) in the header area,
+// after the barriers, counters and descriptors.
+constexpr uint32_t kPlanOff = 4352;
+static_assert(16 * kVarlenSlots + 4 * (4 + kVarlenSlots) + kVarlenSlots * kDescStride + 15 <= kPlanOff &&
+                  kPlanOff + 64 * 16 <= kVarlenChunkHdr,
+              "header layout");
 
 // What one tile needs: its batch row, length, heads and shared-memory bases.
 struct TileRef {
@@ -161,24 +174,24 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
     const int hkv = P.num_heads_kv;
     const uint64_t policy = policy_evict_first();
     int64_t tail = 0, head = 0;  // ring bytes ever allocated / ever released
+    uint32_t off = 0;            // ring position of `tail` (tail mod R, kept incrementally)
     int c = 0, oldest = 0, tiles = 0;
     bool stop = false;
+    // Plan of the current 32-row window: per row {bytes, length, kind,
+    // tiles}; per chunk {first row, rows, K/V rows, tiles | kind << 24}.
+    int4* win = reinterpret_cast<int4*>(smem + kPlanOff);
+    int4* cinfo = win + 32;
     auto heads_per_tile = [](int s_len) {
       const int s = s_len <= 1 ? 1 : s_len <= 2 ? 2 : s_len <= 4 ? 4 : s_len <= 8 ? 8 : 16;
       return 16 / s;
     };
-    // Pending multi-row chunk; lane j keeps row j's length, relative K row
-    // and first tile.
-    int pn = 0, p_rows = 0, p_tiles = 0, p_c0 = 0;
-    int64_t p_b0 = 0;
-    int my_s = 0, my_krow = 0, my_tstart = 0;
 
-    // Allocates ring space and a slot for a chunk, writes its descriptor
-    // (lanes j < nrows write their row entries), arms `full` and publishes
-    // the chunk after `issue` has launched its copies.
-    auto emit = [&](int64_t b0, int nrows, int h0, int nh, int ntiles, uint32_t kvb,
-                    uint32_t qb, int s_row, int krow, int tstart, auto&& issue) {
-      const uint32_t sz = 2 * kvb + qb;  // whole rows: a multiple of D*2 bytes
+    // Allocates ring space and a slot for a chunk, lets `rows` write the
+    // descriptor's per-row entries, writes its header, arms `full`, lets
+    // `issue` launch the copies and publishes the chunk.
+    auto emit = [&](int64_t b0, int nrows, int h0, int nh, int ntiles, uint32_t kvb, uint32_t qb,
+                    auto&& rows, auto&& issue) {
+      const uint32_t sz = 2 * kvb + qb;  // whole rows: a multiple of D*2 bytes, <= R/2
       while (oldest <= c - M || tail + sz - head > (int64_t)R) {
         if (!mbar_wait(empty0 + 8u * (oldest % M), (oldest / M) & 1, abort_flag, P.err,
                        P.wait_timeout_ns, kSiteProducerEmpty)) {
@@ -188,20 +201,18 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
         head = desc_at(oldest % M)->end_total;
         ++oldest;
       }
-      const uint32_t off = (uint32_t)(tail % R);
+      const uint32_t at = off;
       tail += sz;
+      off += sz;
+      if (off >= R) off -= R;
       const int slot = c % M;
       const uint32_t bar = full0 + 8u * slot;
       ChunkDesc* d = desc_at(slot);
-      if (lane < nrows) {
-        d->krow[lane] = (uint16_t)krow;
-        d->s_len[lane] = (uint16_t)s_row;
-        d->tstart[lane] = (uint16_t)tstart;
-      }
+      rows(d);
       if (lane == 0) {
         d->b0 = b0;
         d->end_total = tail;
-        d->off = off;
+        d->off = at;
         d->kv_bytes = kvb;
         d->h0 = h0;
         d->nh = nh;
@@ -210,9 +221,9 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
         d->nrows = nrows;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(bar, 2 * kvb + qb);  // releases the descriptor
+      if (lane == 0) mbar_arrive_expect_tx(bar, sz);  // releases the descriptor
       __syncwarp();
-      issue(off, bar);
+      issue(at, bar);
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
@@ -222,7 +233,7 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
       ++c;
     };
 
-    // Bulk copy of len bytes to ring offset off (< R), split in two where it
+    // Bulk copy of len bytes to ring offset off (< 2R), split in two where it
     // runs past the end of the ring.
     auto copy_to_ring = [&](uint32_t off, const uint16_t* src, uint32_t len, uint32_t bar) {
       if (off >= R) off -= R;
@@ -231,72 +242,124 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
       if (first < len) bulk_g2s(ring0, src + first / 2, len - first, bar, policy);
     };
 
-    auto flush = [&]() {
-      if (pn == 0 || stop) return;
-      const uint32_t kvb = (uint32_t)p_rows * hkv * (D * 2);
-      const uint32_t qb = (uint32_t)(pn * hkv * G) * (D * 2);
-      const int64_t ksrc = (int64_t)p_c0 * hkv * D;
-      const int64_t qsrc = p_b0 * hkv * G * D;
-      emit(p_b0, pn, 0, hkv, p_tiles, kvb, qb, my_s, my_krow, my_tstart,
-           [&](uint32_t dst, uint32_t bar) {
-             if (lane == 0 && kvb) copy_to_ring(dst, P.K + ksrc, kvb, bar);
-             if (lane == 1 && kvb) copy_to_ring(dst + kvb, P.V + ksrc, kvb, bar);
-             if (lane == 2) copy_to_ring(dst + 2 * kvb, P.Q + qsrc, qb, bar);
-           });
-      pn = p_rows = p_tiles = 0;
-    };
+    for (int64_t base = row_lo; base < row_hi && !stop; base += 32) {
+      // One row per lane: length, bytes, tiles and kind (0 whole row, 1 too
+      // long for a chunk: head groups, 2 invalid length).
+      const int nrow = row_hi - base < 32 ? (int)(row_hi - base) : 32;
+      int c0 = 0, c1 = 0;
+      if (lane < nrow) {
+        c0 = __ldg(P.cu_seqlens + base + lane);
+        c1 = __ldg(P.cu_seqlens + base + lane + 1);
+      }
+      const int s_len = c1 - c0;
+      int kind = 0, rt = 0;
+      uint64_t rb = 0;
+      if (s_len < 0 || s_len > P.max_seqlen) {
+        kind = 2;
+      } else {
+        const int nu = heads_per_tile(s_len);
+        rb = (uint64_t)(2 * s_len + G) * (D * 2) * (uint64_t)hkv;
+        rt = (hkv + nu - 1) / nu;
+        if (rb > P.chunk_max) kind = 1;
+      }
+      win[lane] = make_int4((int)(rb < 0x7fffffffu ? rb : 0x7fffffffu), s_len, kind, rt);
+      __syncwarp();
+      // Greedy packing of consecutive whole rows into chunks (at most
+      // kChunkRows rows and chunk_max bytes each), run by every lane over the
+      // window; rows of kind 1 and 2 are entries of their own. Each lane keeps
+      // its row's chunk, index in it, first K/V row and first tile.
+      int k = -1, pn = 0, p_rows = 0, p_tiles = 0;
+      uint32_t pend = 0;
+      int my_k = 0, my_j = 0, my_krow = 0, my_tstart = 0;
+      for (int j = 0; j < nrow; ++j) {
+        const int4 w = win[j];
+        if (w.z != 0) {
+          ++k;
+          pn = 0;
+          if (j == lane) my_k = k;
+          continue;
+        }
+        if (pn == 0 || pn == kChunkRows || pend + (uint32_t)w.x > P.chunk_max) {
+          ++k;
+          pn = p_rows = p_tiles = 0;
+          pend = 0;
+        }
+        if (j == lane) {
+          my_k = k;
+          my_j = pn;
+          my_krow = p_rows;
+          my_tstart = p_tiles;
+        }
+        ++pn;
+        pend += (uint32_t)w.x;
+        p_rows += w.y;
+        p_tiles += w.w;
+      }
+      // The last row of each entry records it.
+      const int next_k = __shfl_down_sync(kFullMask, my_k, 1);
+      if (lane < nrow && (lane == nrow - 1 || next_k != my_k))
+        cinfo[my_k] = make_int4(lane - my_j, my_j + 1, my_krow + (kind == 0 ? s_len : 0),
+                                (my_tstart + rt) | (kind << 24));
+      __syncwarp();
 
-    for (int64_t base = row_lo; base < row_hi && !stop; base += 31) {
-      const int64_t idx = base + lane;
-      const int cu_l = idx <= row_hi ? __ldg(P.cu_seqlens + idx) : 0;
-      const int nrows = row_hi - base < 31 ? (int)(row_hi - base) : 31;
-      for (int i = 0; i < nrows && !stop; ++i) {
-        const int c0 = __shfl_sync(kFullMask, cu_l, i);
-        const int s_len = __shfl_sync(kFullMask, cu_l, i + 1) - c0;
-        const int64_t b = base + i;
-        if (s_len < 0 || s_len > P.max_seqlen) {
-          flush();  // chunks hold consecutive rows only
+      for (int q = 0; q <= k && !stop; ++q) {
+        const int4 ci = cinfo[q];
+        const int first = ci.x;
+        const int ckind = ci.w >> 24;
+        const int64_t b0 = base + first;
+        const int cc0 = __shfl_sync(kFullMask, c0, first);
+        const int sl0 = __shfl_sync(kFullMask, s_len, first);
+        if (ckind == 2) {  // chunks hold consecutive valid rows only
           if (lane == 0) report_device_error(P.err, 1u /* FMHA_ERR_INVALID_ARG */, 5u);
           continue;
         }
-        const int nu = heads_per_tile(s_len);
-        const uint32_t per_head = (uint32_t)(2 * s_len + G) * (D * 2);
-        const uint32_t row_bytes = per_head * hkv;
-        if (row_bytes <= P.chunk_max) {
-          // Whole row: append to the pending chunk (flush first if full).
-          const uint32_t pend = (uint32_t)(2 * p_rows + pn * G) * hkv * (D * 2);
-          if (pn == kChunkRows || (pn > 0 && pend + row_bytes > P.chunk_max)) flush();
-          if (stop) break;
-          if (pn == 0) {
-            p_b0 = b;
-            p_c0 = c0;
-          }
-          if (lane == pn) {
-            my_s = s_len;
-            my_krow = c0 - p_c0;
-            my_tstart = p_tiles;
-          }
-          ++pn;
-          p_rows += s_len;
-          p_tiles += (hkv + nu - 1) / nu;
+        if (ckind == 0) {
+          const uint32_t kvb = (uint32_t)ci.z * hkv * (D * 2);
+          const uint32_t qb = (uint32_t)(ci.y * hkv * G) * (D * 2);
+          const int64_t ksrc = (int64_t)cc0 * hkv * D;
+          const int64_t qsrc = b0 * hkv * G * D;
+          emit(b0, ci.y, 0, hkv, ci.w & 0xffffff, kvb, qb,
+               [&](ChunkDesc* d) {
+                 if (lane < nrow && my_k == q) {
+                   d->krow[my_j] = (uint16_t)my_krow;
+                   d->s_len[my_j] = (uint16_t)s_len;
+                   d->tstart[my_j] = (uint16_t)my_tstart;
+                 }
+               },
+               [&](uint32_t dst, uint32_t bar) {
+                 // Lanes 0, 1, 2 copy K, V and Q together.
+                 if (lane < 3) {
+                   const uint16_t* src = lane == 0 ? P.K + ksrc : lane == 1 ? P.V + ksrc : P.Q + qsrc;
+                   const uint32_t len = lane < 2 ? kvb : qb;
+                   if (len) copy_to_ring(dst + lane * kvb, src, len, bar);
+                 }
+               });
           continue;
         }
         // Row too long on its own: head groups with one copy per position.
-        flush();
+        const int nu = heads_per_tile(sl0);
+        const uint32_t per_head = (uint32_t)(2 * sl0 + G) * (D * 2);
         int nh_max = (int)(P.chunk_max / per_head);
         if (nh_max < 1) nh_max = 1;
         if (nh_max > hkv) nh_max = hkv;
         if (nh_max >= nu) nh_max -= nh_max % nu;  // whole tiles per group
         for (int h0 = 0; h0 < hkv && !stop; h0 += nh_max) {
           const int nh = hkv - h0 < nh_max ? hkv - h0 : nh_max;
-          const uint32_t kvb = (uint32_t)s_len * nh * (D * 2);
+          const uint32_t kvb = (uint32_t)sl0 * nh * (D * 2);
           const uint32_t qb = (uint32_t)(nh * G) * (D * 2);
           const uint32_t run = (uint32_t)nh * (D * 2);
-          const int64_t qsrc = (b * hkv + h0) * G * D;
-          emit(b, 1, h0, nh, (nh + nu - 1) / nu, kvb, qb, s_len, 0, 0,
+          const int64_t qsrc = (b0 * hkv + h0) * G * D;
+          emit(b0, 1, h0, nh, (nh + nu - 1) / nu, kvb, qb,
+               [&](ChunkDesc* d) {
+                 if (lane == 0) {
+                   d->krow[0] = 0;
+                   d->s_len[0] = (uint16_t)sl0;
+                   d->tstart[0] = 0;
+                 }
+               },
                [&](uint32_t dst, uint32_t bar) {
-                 if (lane < s_len) {
-                   const int64_t ksrc = ((int64_t)(c0 + lane) * hkv + h0) * D;
+                 if (lane < sl0) {
+                   const int64_t ksrc = ((int64_t)(cc0 + lane) * hkv + h0) * D;
                    copy_to_ring(dst + lane * run, P.K + ksrc, run, bar);
                    copy_to_ring(dst + kvb + lane * run, P.V + ksrc, run, bar);
                  }
@@ -304,8 +367,8 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
                });
         }
       }
+      __syncwarp();  // the plan arrays are rewritten by the next window
     }
-    flush();
     if (lane == 0) {
       __threadfence_block();
       if (!stop) *total_tiles = tiles;
