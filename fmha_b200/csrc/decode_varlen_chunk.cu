@@ -55,9 +55,6 @@ namespace fmha {
 namespace {
 
 constexpr int kChunkRows = 8;  // whole batch rows per chunk at most
-#ifndef FMHA_VARLEN_SPIN_NS
-#define FMHA_VARLEN_SPIN_NS 128
-#endif  // whole batch rows per chunk at most
 
 struct alignas(16) ChunkDesc {
   int64_t b0;         // first batch row
