@@ -424,6 +424,10 @@ __device__ __forceinline__ float dot8f(const float (&q)[8], const float (&k)[8])
 // of tile unit u, the unit of the lane's slot us; store(u, acc): called once per (slot, lane) with the lane's 8
 // output columns of every head of unit u -- the caller stores when
 // u < units_valid and writer() holds. Same math as attend_tile.
+template <int D, int SMAX, int G, class LoadV, class Store>
+__device__ __forceinline__ void tile16_softmax_pv(LoadV loadV, Store store, int s_len,
+                                                  int units_valid, float* sc, int lane);
+
 template <int D, int SMAX, int G, class LoadK, class LoadV, class LoadQ, class Store>
 __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ loadQ, Store store,
                                               int s_len, int units_valid, float scale_log2,
@@ -469,6 +473,22 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
         sc[(gb + g) * T::ROWS + r0 * T::NP + pi] = row_ok(pi) ? s * scale_log2 : -INFINITY;
     }
   }
+  tile16_softmax_pv<D, SMAX, G>(loadV, store, s_len, units_valid, sc, lane);
+}
+
+// Softmax over the scores in `sc` (sc[g*16 + r], already scaled by
+// log2(e)*scale, -inf for masked rows) and P.V of one 16-row tile on the CUDA
+// cores; the second half of attend_tile16, shared with attend_tile16_mq.
+template <int D, int SMAX, int G, class LoadV, class Store>
+__device__ __forceinline__ void tile16_softmax_pv(LoadV loadV, Store store, int s_len,
+                                                  int units_valid, float* sc, int lane) {
+  using T = Tile16<D, SMAX, G>;
+  const int r0 = lane / T::LPR;
+  auto row_ok = [&](int p) {
+    const int r = r0 * T::NP + p;
+    return (r % SMAX) < s_len && (r / SMAX) < units_valid;
+  };
+  auto slot_unit = [&](int us) { return (r0 * T::NP + us * T::SPL) / SMAX; };
   __syncwarp();
 
 #pragma unroll
@@ -514,6 +534,85 @@ __device__ __forceinline__ void attend_tile16(LoadK loadK, LoadV loadV, LoadQ lo
     }
     if (!T::CROSS || r0 == 0) store(slot_unit(us), acc);
   }
+}
+
+__device__ __forceinline__ void mma_16816_rows(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// attend_tile16 with the scores on the tensor cores (mma.sync m16n8k16, bf16
+// operands, fp32 accumulation; the products are exact): M = the tile's 16 K
+// rows, N = its NU*G query rows (one or two n-tiles), K = D. Lane (g, t)
+// loads 16 contiguous bytes of K rows g and g+8 and of query row g (+8) at
+// column 32j + 8t; the dot product's order is free, so those 8 columns are
+// the lane's k slots of two k-steps in A and B alike. Of C only the entries
+// C[r][(unit(r), h)] are kept: each is a separate dot product, so rows and
+// query rows of other units (or garbage past the tile) never mix into them.
+// krow(r): shared address of tile row r (row base, no column offset);
+// qrow(u, h): shared address of query head h of tile unit u. Softmax and P.V
+// as in attend_tile16.
+template <int D, int SMAX, int G>
+struct Tile16Mq {
+  static constexpr int NU = 16 / SMAX;
+  static constexpr int NQ = NU * G;
+  static constexpr int NT = (NQ + 7) / 8;
+  static constexpr bool OK = NQ <= 16;  // at most two n-tiles
+};
+
+template <int D, int SMAX, int G, class KRow, class QRow, class LoadV, class Store>
+__device__ __forceinline__ void attend_tile16_mq(KRow krow, QRow qrow, LoadV loadV, Store store,
+                                                 int s_len, int units_valid, float scale_log2,
+                                                 float* sc, int lane) {
+  using M = Tile16Mq<D, SMAX, G>;
+  static_assert(M::OK, "at most 16 query rows per tile");
+  const int g = lane >> 2, t = lane & 3;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  const int rA = g, rB = g + 8;
+  const bool okA = (rA % SMAX) < s_len && (rA / SMAX) < units_valid;
+  const bool okB = (rB % SMAX) < s_len && (rB / SMAX) < units_valid;
+  const uint32_t col = (uint32_t)t * 16;
+  const uint32_t kA = krow(rA) + col, kB = krow(rB) + col;
+  uint32_t qa[M::NT];
+  bool qok[M::NT];
+#pragma unroll
+  for (int nt = 0; nt < M::NT; ++nt) {
+    const int n = g + 8 * nt;
+    qok[nt] = n < M::NQ && n / G < units_valid;
+    qa[nt] = qok[nt] ? qrow(n / G, n % G) + col : 0u;
+  }
+  float c[M::NT][4];
+#pragma unroll
+  for (int nt = 0; nt < M::NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[nt][i] = 0.0f;
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) {
+    const uint4 a = okA ? lds128(kA + 64 * j) : z;
+    const uint4 b = okB ? lds128(kB + 64 * j) : z;
+#pragma unroll
+    for (int nt = 0; nt < M::NT; ++nt) {
+      const uint4 q = qok[nt] ? lds128(qa[nt] + 64 * j) : z;
+      mma_16816_rows(c[nt], a.x, b.x, a.y, b.y, q.x, q.y);
+      mma_16816_rows(c[nt], a.z, b.z, a.w, b.w, q.z, q.w);
+    }
+  }
+  // c[nt][0..1]: row g, query rows n = 8nt + 2t + {0,1}; c[nt][2..3]: row g+8.
+#pragma unroll
+  for (int nt = 0; nt < M::NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int n = 8 * nt + 2 * t + (e & 1);
+      const int r = e < 2 ? rA : rB;
+      if (n < M::NQ && n / G == r / SMAX)
+        sc[(n % G) * 16 + r] = (e < 2 ? okA : okB) ? c[nt][e] * scale_log2 : -INFINITY;
+    }
+  tile16_softmax_pv<D, SMAX, G>(loadV, store, s_len, units_valid, sc, lane);
 }
 
 // ----------------------------------------------------------------------

@@ -121,6 +121,17 @@ __device__ __forceinline__ void chunk_tile(const VarlenParams& P, const TileRef&
 #pragma unroll
     for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
   };
+#ifndef FMHA_CHUNK_NO_MQ
+  if constexpr (Tile16Mq<D, SMAX, G>::OK) {
+    auto base = [&](uint32_t off) { return ring0 + (off >= R ? off - R : off); };
+    auto krow = [&](int r) {
+      return base(c.koff + (uint32_t)((r % SMAX) * nh + hl0 + r / SMAX) * (D * 2));
+    };
+    auto qrow = [&](int u, int h) { return base(c.qoff + (uint32_t)((hl0 + u) * G + h) * (D * 2)); };
+    attend_tile16_mq<D, SMAX, G>(krow, qrow, loadV, store, c.s_len, nv, P.scale_log2, sc, lane);
+    return;
+  }
+#endif
   attend_tile16<D, SMAX, G>(loadK, loadV, loadQ, store, c.s_len, nv, P.scale_log2, sc, lane);
 }
 

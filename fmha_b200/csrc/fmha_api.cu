@@ -376,12 +376,11 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
                                             : 1.0 / std::sqrt((double)head_dim);
   P.scale_log2 = (float)(1.4426950408889634 * scale);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  // FMHA_VARLEN_KERNEL=ldg|chunk overrides the per-head_dim default below.
-  // Default per head_dim (measured on the reference's Poisson(4) table):
-  // D=256 -> the register-prefetch kernel with 4-head work items (16 KB tiles
-  // leave the shared-memory ring too few in flight); D=128 -> the chunk ring.
+  // Default: the chunk ring for both head_dims (on the reference's Poisson(4)
+  // table it beats the register-prefetch kernel by 4-27 % at D=256 once its
+  // scores run on the tensor cores). FMHA_VARLEN_KERNEL=ldg|chunk overrides.
   static const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
-  const bool use_ldg = (kind && *kind) ? std::strcmp(kind, "ldg") == 0 : head_dim == 256;
+  const bool use_ldg = (kind && *kind) ? std::strcmp(kind, "ldg") == 0 : false;
   if (use_ldg) {
     int bps = 1;
     st = blocks_per_sm(reinterpret_cast<const void*>(fn), kLdgThreads, &bps);
