@@ -157,3 +157,44 @@ def test_varlen_full_size_reference_seqlens(cuda, oracle, hq, d):
         ref32, _ = oracle.decode_thd(q, k, v, np.array([0, s], np.int32), 1, hq, hq, d)
         got = O[b0 * hq * d:(b0 + 1) * hq * d].cpu().view(cuda.int16).numpy().view(np.uint16)
         check_close(got, ref32)
+
+
+PLAN_CASES = [  # (hq, hkv, d, chunk byte limit or 0 for the default, max_seqlen_kv)
+    (16, 16, 128, 0, 16),
+    (16, 16, 128, 20480, 16),   # most rows split into head groups
+    (32, 16, 256, 0, 16),       # GQA
+    (32, 16, 256, 40960, 12),   # splits + rows longer than max_seqlen_kv mid-window
+    (4, 4, 128, 0, 16),         # tiny rows: the 8-rows-per-chunk limit binds
+    (8, 1, 128, 0, 16),         # one kv head: many chunks, descriptor slots recycle fast
+]
+
+
+@pytest.mark.parametrize("hq,hkv,d,chunk,max_s", PLAN_CASES, ids=str)
+def test_varlen_chunk_planning_all_rows(cuda, oracle, monkeypatch, hq, hkv, d, chunk, max_s):
+    """Enough rows that every CTA plans several 32-row windows, packs rows into
+    chunks and wraps its ring many times; lengths mix Poisson(4) with 0, 1,
+    16 and (when max_seqlen_kv < 16) rows that must be flagged and skipped.
+    Every row is checked against the oracle."""
+    if chunk:
+        monkeypatch.setenv("FMHA_VARLEN_CHUNK", str(chunk))
+    b = 148 * (40 if d == 128 else 33)
+    rng = np.random.default_rng(hq * 1000 + hkv * 10 + d + chunk)
+    x = rng.poisson(4, size=4 * b)
+    sl = x[(x >= 2) & (x <= 16)][:b].astype(np.int32)
+    pos = rng.choice(b, size=b // 10, replace=False)
+    sl[pos] = rng.choice(np.array([0, 1, 16, 16], np.int32), size=pos.size)
+    t = int(sl.sum())
+    q = oracle.gen_bf16(b * hq * d, 77, 1)
+    k = oracle.gen_bf16(t * hkv * d, 77, 2)
+    v = oracle.gen_bf16(t * hkv * d, 77, 3)
+    out, err, cu = run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, max_s=max_s)
+    bad = sl > max_s
+    if bad.any():
+        assert err & 0xff == fmha_b200.FMHA_ERR_INVALID_ARG and (err >> 8) == 5
+    else:
+        assert err == 0
+    ref32, _ = oracle.decode_thd(q, k, v, cu, b, hq, hkv, d)
+    n = hq * d
+    rows_ok = np.repeat(~bad, n)
+    check_close(out[rows_ok], ref32[rows_ok])
+    assert np.all(out[~rows_ok] == POISON)
