@@ -198,3 +198,48 @@ def test_varlen_chunk_planning_all_rows(cuda, oracle, monkeypatch, hq, hkv, d, c
     rows_ok = np.repeat(~bad, n)
     check_close(out[rows_ok], ref32[rows_ok])
     assert np.all(out[~rows_ok] == POISON)
+
+
+def test_varlen_negative_lengths_cover_every_valid_row(cuda, oracle):
+    """cu_seqlens that is not monotonic (a few negative lengths) makes the
+    byte-balanced CTA ranges irregular; every valid row must still be
+    computed (no gaps), invalid rows flagged and left untouched."""
+    b, hq, hkv, d = 148 * 12, 16, 16, 128
+    rng = np.random.default_rng(5)
+    x = rng.poisson(4, size=4 * b)
+    sl = x[(x >= 2) & (x <= 16)][:b].astype(np.int32)
+    neg = rng.choice(np.arange(10, b), size=20, replace=False)
+    sl[neg] = -3
+    cu = np.concatenate([[0], np.cumsum(sl)]).astype(np.int32)
+    assert cu.min() >= 0
+    t = int(cu.max())
+    q = oracle.gen_bf16(b * hq * d, 9, 1)
+    k = oracle.gen_bf16(t * hkv * d, 9, 2)
+    v = oracle.gen_bf16(t * hkv * d, 9, 3)
+    n = b * hq * d
+    Q, K, V = to_dev(cuda, q), to_dev(cuda, k), to_dev(cuda, v)
+    CU = cuda.from_numpy(cu).cuda()
+    buf = cuda.full((n + 2 * GUARD,), POISON, dtype=cuda.int16, device="cuda")
+    lib = fmha_b200.load()
+    st = lib.fmha_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                 buf[GUARD:GUARD + n].data_ptr(), CU.data_ptr(), b, hq, hkv, 16, d,
+                                 0.0, None)
+    assert st == 0
+    cuda.cuda.synchronize()
+    err = fmha_b200.device_error()
+    assert err & 0xff == fmha_b200.FMHA_ERR_INVALID_ARG and (err >> 8) == 5
+    out = buf.cpu().numpy().view(np.uint16)
+    assert np.all(out[:GUARD] == POISON) and np.all(out[GUARD + n:] == POISON)
+    out = out[GUARD:GUARD + n]
+    m = hq * d
+    kv_row = hkv * d
+    for r in range(b):
+        got = out[r * m:(r + 1) * m]
+        if sl[r] < 0:
+            assert np.all(got == POISON)
+            continue
+        c0, c1 = int(cu[r]), int(cu[r + 1])
+        ref32, _ = oracle.decode_thd(q[r * m:(r + 1) * m], k[c0 * kv_row:c1 * kv_row],
+                                     v[c0 * kv_row:c1 * kv_row], np.array([0, c1 - c0], np.int32),
+                                     1, hq, hkv, d)
+        check_close(got, ref32)
