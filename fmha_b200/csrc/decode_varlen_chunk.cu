@@ -13,7 +13,9 @@
 // are one contiguous run of nh*D elements. Packing short rows together keeps
 // every chunk large, which is what keeps the bulk copies efficient.
 //
-// Per CTA (persistent, one per SM): a contiguous range of batch rows.
+// Per CTA (persistent, one per SM): a contiguous range of batch rows holding
+// an equal share of the bytes (found by a 16-ary search over cu_seqlens, see
+// weight_split), not an equal number of rows.
 //  * Producer (warp 0) plans 32 rows at a time: each lane loads its row's
 //    cu_seqlens pair and sizes the row, then every lane runs the same greedy
 //    packing over the window from shared memory (no shuffle chains), so each
@@ -22,8 +24,7 @@
 //    multiple of one row (D*2 bytes), so a chunk may wrap past the end
 //    without any row straddling it (copies that cross are split in two;
 //    readers wrap their row offsets), and no space is lost to padding; writes
-//    the chunk's
-//    descriptor (per-row lengths, offsets and first tiles) into slot
+//    the chunk's descriptor (per-row lengths, offsets and first tiles) into slot
 //    c % kSlots, arms the slot's `full` mbarrier with the chunk's byte count
 //    and issues the copies: one bulk copy each for K, V and Q of whole rows
 //    (lanes 0-2 together), or one K and one V copy per position for a head
@@ -35,7 +36,8 @@
 //    one chunk) from a shared atomic tile counter, find the tile's chunk among
 //    the published ones, wait for its `full` phase (published => armed, so the
 //    parity names the right phase), run the shared tile math from shared
-//    memory and stream fp16 rows to O. The last tile of a chunk resets the
+//    memory (QK^T on mma.sync when the tile has at most 16 query rows) and
+//    stream fp16 rows to O. The last tile of a chunk resets the
 //    chunk's tile counter and arrives on its `empty` mbarrier.
 //
 // A row length outside [0, max_seqlen_kv] sets the device error word
