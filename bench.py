@@ -140,10 +140,19 @@ class ClockSampler:
         sm = [num(r[1]) for r in rows if num(r[1])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        per_gpu = {}
+        for g in sorted({int(r[0]) for r in rows}):
+            mine = [r for r in rows if int(r[0]) == g]
+            v = [num(r[1]) for r in mine if num(r[1])]
+            per_gpu[str(g)] = {"sm_mhz": statistics.median(v) if v else None,
+                               "sm_mhz_min": min(v) if v else None,
+                               "power_w_max": max(num(r[3]) or 0 for r in mine),
+                               "reasons": sorted({names[i] for r in mine for i in range(4)
+                                                  if r[5 + i] == "Active"})}
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(num(r[2]) or 0 for r in rows),
                 "power_w_max": max(num(r[3]) or 0 for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "per_gpu": per_gpu}
 
 
 # ---------------------------------------------------------------- reference arm
@@ -180,18 +189,15 @@ def run_reference_arm(args, cfg_name, cfg):
         else:
             O.decode_bhsd(q, k, v, nrows, hq, hkv, s, d, want_f32=False)
 
-    # Calibrate a sample whose step takes ~2 s, so K+W steps end in minutes.
-    n = min(b_all, 64)
-    while True:
-        q, k, v = make(n)
-        t0 = time.perf_counter()
-        step(n, q, k, v)
-        dt = time.perf_counter() - t0
-        if dt > 0.5 or n >= b_all:
-            break
-        n = min(b_all, n * 4)
-    target = 2.0 if (args.steps + args.warmup) <= 30 else 60.0 / (args.steps + args.warmup)
-    n = max(1, min(b_all, int(n * target / max(dt, 1e-6))))
+    # The whole batch every step (the CPU work is linear in rows; timing the
+    # full call makes ms_per_step a measurement, not an extrapolation). Only
+    # when the host cannot hold the inputs twice over is a contiguous sample
+    # used, and the line says so.
+    import psutil
+    need = 2 * 2 * (b_all * hq * d + 2 * b_all * hkv * s * d) * (2 if use_ref else 1)
+    n = b_all
+    if psutil.virtual_memory().available < need:
+        n = max(1, int(b_all * psutil.virtual_memory().available / need))
     q, k, v = make(n)
     for _ in range(args.warmup):
         step(n, q, k, v)
@@ -203,14 +209,14 @@ def run_reference_arm(args, cfg_name, cfg):
     sec = sum(times) / len(times)
     tbps = algo_bytes(n, hq, hkv, s, d) / sec / 1e12
     kind = "reference" if use_ref else "port"
-    sample = (f"{n} of {b_all} batch rows per step (contiguous, seed 0); "
+    sample = (f"{n} of {b_all} batch rows per step (seed 0); "
               + ("reference do_validation (bf16 P) built from fmha_host.cpp, one batch slice "
                  "per thread" if use_ref else "oracle restatement (fp32 P), OpenMP over batch"))
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tbps, 6), "unit": "TB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(sec * 1e3 * b_all / n, 3),
-        "ms_per_step_note": "time per sample step scaled to the full batch",
+        "ms_per_step": round(sec * 1e3, 3),
+        "rows_per_step": n,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded bf16 N(0,1) approximation)",
         "config": config_block(cfg_name, cfg, 1),
@@ -288,6 +294,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the all-rows check of the output against the CPU oracle")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="skip the NCCL all-gather of the sharded output (N > 1)")
     ap.add_argument("--no-clocks", action="store_true",
                     help="skip the nvidia-smi sampler (profiling runs)")
     ap.add_argument("--varlen-uniform", type=int, default=0,
@@ -368,14 +378,25 @@ def main():
     if args.batch > 0:
         cfg = (args.batch,) + tuple(cfg[1:])
     varlen = args.config in VARLEN
+    keep = []
     if varlen:
         # The reference's own table: packed K/V, Poisson(4) seqlens (device time
         # only; the e2e and CPU legs are defined for the dense north-star call).
-        r = time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev)
+        r = time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev,
+                        keep=keep)
         args.no_e2e = args.no_cpu = True
     else:
         r = time_config(torch, fmha_b200, cfg, world, rank, args, args.variant, barrier,
-                        max_over_ranks, dev, clocks=not args.no_clocks)
+                        max_over_ranks, dev, clocks=not args.no_clocks, keep=keep)
+    ranks_ms = per_rank(torch, dist, dev, r["kernel_ms"], world)
+    parity = None
+    if not args.no_parity:
+        parity = parity_leg(torch, dist, dev, keep, cfg, world, rank, varlen)
+    gather = None
+    if world > 1 and not args.no_gather:
+        gather = gather_leg(torch, dist, dev, keep[3], cfg, world, rank)
+    del keep
+    torch.cuda.empty_cache()
     e2e = None
     if not args.no_e2e:
         e2e = e2e_leg(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev)
@@ -403,6 +424,9 @@ def main():
                          "traffic": ncu_traffic(args.config),
                          "kernel": "fmha::decode_*_kernel (one launch per step)"},
             "gpu_launches": args.steps,
+            "per_rank_ms": ranks_ms,
+            "parity": parity,
+            "gather": gather,
             "clocks": r["clocks"],
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -412,6 +436,129 @@ def main():
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+ATOL, RTOL = 2e-3, 1e-2   # the library tolerance, against the fp32-P oracle
+PARITY_SLICE_ROWS = 1024
+
+
+def per_rank(torch, dist, dev, ms, world):
+    """Device ms per call of every rank (min / median / max and the list)."""
+    vals = [ms]
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        vals = [float(x.item()) for x in out]
+    return {"min": round(min(vals), 5), "median": round(statistics.median(vals), 5),
+            "max": round(max(vals), 5), "all": [round(v, 5) for v in vals]}
+
+
+def parity_leg(torch, dist, dev, keep, cfg, world, rank, varlen):
+    """Every row of this rank's output against the CPU oracle (the fp32-P
+    restatement of the reference's do_validation, fmha_host.cpp:158-284) on
+    the same inputs, copied back from the device after the timed region, in
+    slices of PARITY_SLICE_ROWS rows. An element passes when |o-r| <= 2e-3 or
+    |o-r| <= 1e-2*|r|; a non-finite output fails. Sums over ranks."""
+    import numpy as np
+    from oracle import oracle as Or
+    _, hq, hkv, s, d = cfg
+    Q, K, V, O = keep[:4]
+    Or.set_threads(max(1, (os.cpu_count() or 1) // world))
+    t0 = time.perf_counter()
+    qn = hq * d
+    b = O.numel() // qn
+
+    def bits(x):
+        return x.cpu().view(torch.int16).numpy().view(np.uint16)
+
+    bad, max_abs = 0, 0.0
+    for r0 in range(0, b, PARITY_SLICE_ROWS):
+        r1 = min(b, r0 + PARITY_SLICE_ROWS)
+        q = bits(Q[r0 * qn:r1 * qn])
+        if varlen:
+            cu = np.asarray(keep[4], dtype=np.int64)
+            c0, c1 = int(cu[r0]), int(cu[r1])
+            k = bits(K[c0 * hkv * d:c1 * hkv * d])
+            v = bits(V[c0 * hkv * d:c1 * hkv * d])
+            ref, _ = Or.decode_thd(q, k, v, (cu[r0:r1 + 1] - c0).astype(np.int32), r1 - r0, hq,
+                                   hkv, d)
+        else:
+            kn = hkv * s * d
+            k = bits(K[r0 * kn:r1 * kn])
+            v = bits(V[r0 * kn:r1 * kn])
+            ref, _ = Or.decode_bhsd(q, k, v, r1 - r0, hq, hkv, s, d)
+        o = bits(O[r0 * qn:r1 * qn]).view(np.float16).astype(np.float32)
+        err = np.abs(o - ref)
+        ok = np.isfinite(o) & ((err <= ATOL) | (err <= RTOL * np.abs(ref)))
+        bad += int((~ok).sum())
+        max_abs = max(max_abs, float(np.nanmax(err)) if err.size else 0.0)
+    sec = time.perf_counter() - t0
+    rows, elems = b, b * qn
+    if dist is not None:
+        t = torch.tensor([rows, elems, bad], dtype=torch.int64, device=dev)
+        dist.all_reduce(t)
+        rows, elems, bad = (int(x) for x in t.tolist())
+        m = torch.tensor([max_abs, sec], dtype=torch.float64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        max_abs, sec = (float(x) for x in m.tolist())
+    return {"rows": rows, "elements": elems, "bad": bad, "max_abs": float(f"{max_abs:.3e}"),
+            "rule": "|o-r| <= 2e-3 or |o-r| <= 1e-2*|r| vs the fp32-P oracle, every row",
+            "check_s": round(sec, 2)}
+
+
+def gather_leg(torch, dist, dev, O, cfg, world, rank):
+    """All-gather of the sharded O over NCCL (fmha_b200.multi.gather_output),
+    device-timed, max over ranks, then checked: every rank's slice of the
+    gathered tensor must equal that rank's own shard bit for bit (compared
+    through two int64 checksums all-gathered from the ranks)."""
+    from fmha_b200.multi import gather_output, make_shard
+    b_all, hq, hkv, s, d = cfg
+    sh = make_shard(b_all, hq, hkv, s, d, world, rank)
+
+    def checksum(x):
+        v = x.reshape(-1).view(torch.int16).to(torch.int64)
+        w = torch.arange(v.numel(), device=v.device, dtype=torch.int64) % 65521 + 1
+        return torch.stack([v.sum(), (v * w).sum()])
+
+    full = gather_output(O, sh)  # warm-up (NCCL communicator set-up)
+    del full
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    full = gather_output(O, sh)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    mine = checksum(O)
+    sums = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(sums, mine)
+    ok = full.numel() == b_all * hq * d
+    for r in range(world):
+        lo, hi = shard_rows_(b_all, world, r)
+        part = full[lo * hq * d:hi * hq * d]
+        ok = ok and bool(torch.equal(checksum(part), sums[r]))
+    ok = ok and bool(torch.equal(full[sh.o_offset:sh.o_offset + O.numel()].view(torch.int16),
+                                 O.view(torch.int16)))
+    t = torch.tensor([0 if ok else 1], dtype=torch.int64, device=dev)
+    dist.all_reduce(t)
+    m = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(m, op=dist.ReduceOp.MAX)
+    ms = float(m.item())
+    nbytes = full.numel() * full.element_size()
+    del full
+    return {"ok": int(t.item()) == 0, "ms": round(ms, 4), "bytes": nbytes,
+            "algbw_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "busbw_gbs": round(nbytes * (world - 1) / world / (ms * 1e-3) / 1e9, 1),
+            "how": "NCCL all-gather of the fp16 O shards (torch.distributed), max over ranks"}
+
+
+def shard_rows_(b_all, world, rank):
+    from fmha_b200.multi import shard_rows
+    return shard_rows(b_all, world, rank)
 
 
 def shard(b_all, world, rank):
@@ -433,7 +580,10 @@ def alloc_inputs(torch, fmha_b200, cfg, lo, hi, dev):
 
 
 def time_config(torch, fmha_b200, cfg, world, rank, args, variant, barrier, max_over_ranks, dev,
-                clocks):
+                clocks, keep=None):
+    """Device time of K back-to-back calls on this rank's shard. When `keep`
+    is a list, the first input set and its output (Q, K, V, O) are appended
+    to it for the parity and gather checks after timing."""
     b_all, hq, hkv, s, d = cfg
     lo, hi = shard(b_all, world, rank)
     b = hi - lo
@@ -480,13 +630,18 @@ def time_config(torch, fmha_b200, cfg, world, rank, args, variant, barrier, max_
         raise RuntimeError("device error word set during the timed region")
     ms_max = max_over_ranks(ms)
     total = algo_bytes(b_all, hq, hkv, s, d)
+    r = {"value": round(total / (ms_max * 1e-3) / 1e12, 4), "ms_per_step": round(ms_max, 5),
+         "kernel_ms": ms, "clocks": clk}
+    if keep is not None:
+        call(0)  # set 0's O from one more call, outside the timed region
+        torch.cuda.synchronize(dev)
+        keep.extend(sets[0])
     del sets
     torch.cuda.empty_cache()
-    return {"value": round(total / (ms_max * 1e-3) / 1e12, 4), "ms_per_step": round(ms_max, 5),
-            "kernel_ms": ms, "clocks": clk}
+    return r
 
 
-def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev):
+def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev, keep=None):
     """fmha_forward_varlen on the reference's packed layout and seqlens; this
     rank's batch shard. Bytes: Q + K + V (sum of seqlens) + O."""
     import numpy as np
@@ -535,6 +690,8 @@ def time_varlen(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_rank
     ms_max = max_over_ranks(ms)
     total_rows = int(cu_all[-1])
     total = 2 * b_all * hq * d + 4 * total_rows * hkv * d + 2 * b_all * hq * d
+    if keep is not None:
+        keep.extend([Q, K, V, O, cu_all[lo:hi + 1] - t0_row])
     del Q, K, V, O
     torch.cuda.empty_cache()
     return {"value": round(total / (ms_max * 1e-3) / 1e12, 4), "ms_per_step": round(ms_max, 5),
@@ -554,6 +711,27 @@ def local_gpu_index(dev, r):
 E2E_SLICES = 8
 
 
+def bind_to_gpu_cpus(dev, local_rank):
+    """Binds the calling thread to the CPUs NVML reports as local to this GPU
+    (intersected with the CPUs the process may use). Returns (previous
+    affinity or None, a short description)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(local_gpu_index(dev, local_rank))
+        ncpu = os.cpu_count() or 1
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (ncpu + 63) // 64)
+        local = {w * 64 + i for w, m in enumerate(words) for i in range(64) if (int(m) >> i) & 1}
+        before = os.sched_getaffinity(0)
+        cpus = local & before
+        if not cpus or cpus == before:
+            return None, f"unbound ({len(before)} cpus; NVML-local {len(local)})"
+        os.sched_setaffinity(0, cpus)
+        return before, f"bound to {len(cpus)} NVML-local cpus of {len(before)}"
+    except Exception as e:  # NVML missing or unsupported: leave the thread unbound
+        return None, f"unbound ({type(e).__name__})"
+
+
 def e2e_leg(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, dev):
     """The same call through the C ABI with HOST buffers: each step copies
     this shard's Q/K/V from pinned host memory to the device, runs
@@ -562,6 +740,9 @@ def e2e_leg(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, d
     b_all, hq, hkv, s, d = cfg
     lo, hi = shard(b_all, world, rank)
     b = hi - lo
+    # Host buffers are pinned from a thread bound to the GPU's NUMA-local
+    # cores, so their pages land on the node next to the GPU's PCIe root.
+    saved_aff, numa = bind_to_gpu_cpus(dev, int(os.environ.get("LOCAL_RANK", "0")))
     Q, K, V, O = alloc_inputs(torch, fmha_b200, cfg, lo, hi, dev)
     need = 2 * (Q.numel() + K.numel() + V.numel() + O.numel())
     if psutil.virtual_memory().available < 1.5 * need * world:
@@ -626,13 +807,23 @@ def e2e_leg(torch, fmha_b200, cfg, world, rank, args, barrier, max_over_ranks, d
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.e2e_steps)
+    my_ms = ev0.elapsed_time(ev1) / args.e2e_steps
+    ms = max_over_ranks(my_ms)
     h2d = 2 * (Q.numel() + K.numel() + V.numel())
     d2h = 2 * O.numel()
+    dist_ = None
+    if world > 1:
+        import torch.distributed as dist_
+    ranks = per_rank(torch, dist_, dev, my_ms, world)
+    ranks["h2d_gbs_min"] = round(h2d / (ranks["max"] * 1e-3) / 1e9, 1)
+    ranks["h2d_gbs_max"] = round(h2d / (ranks["min"] * 1e-3) / 1e9, 1)
     del Q, K, V, O, hQ, hK, hV, hO
     torch.cuda.empty_cache()
+    if saved_aff is not None:
+        os.sched_setaffinity(0, saved_aff)
     return {"value": round(algo_bytes(b_all, hq, hkv, s, d) / (ms * 1e-3) / 1e12, 5),
             "unit": "TB/s", "ms_per_step": round(ms, 3), "steps": args.e2e_steps,
+            "per_rank_ms": ranks, "numa": numa,
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
             "note": f"pinned host buffers; each step H2D of Q/K/V, fmha_forward and D2H of O "
                     f"over {nsl} batch slices pipelined on three streams"}

@@ -13,8 +13,8 @@ Layout (the reference's Q/O layout, with K/V in [B,H,S,D]):
 from __future__ import annotations
 
 from ._lib import (FMHA_ERR_CUDA, FMHA_ERR_DEVICE_TIMEOUT, FMHA_ERR_INVALID_ARG,  # noqa: F401
-                   FMHA_ERR_MISALIGNED, FMHA_ERR_UNSUPPORTED, FMHA_OK, VARIANTS, FmhaError,
-                   check, load, status_string)
+                   FMHA_ERR_MISALIGNED, FMHA_ERR_UNSUPPORTED, FMHA_OK, VARIANT_AUTO,
+                   VARIANT_BULK, VARIANT_LDG, VARIANTS, FmhaError, check, load, status_string)
 
 __all__ = ["fmha_forward", "fmha_forward_ptr", "fmha_forward_varlen_ptr", "seqlens_poisson", "fill_normal_bf16", "device_error", "FmhaError",
            "load", "version"]
@@ -97,13 +97,20 @@ def seqlens_poisson(batch: int, max_seqlen_kv: int = 16, seed: int = 42, lam: fl
     return out
 
 
+VARLEN_KERNELS = {"auto": VARIANT_AUTO, "chunk": VARIANT_BULK, "ldg": VARIANT_LDG}
+
+
 def fmha_forward_varlen_ptr(q, k, v, o, cu_seqlens, batch, num_heads_q, num_heads_kv,
-                            max_seqlen_kv, head_dim, softmax_scale=0.0, stream=None) -> int:
-    """Raw C call of fmha_forward_varlen; returns the status."""
-    return load().fmha_forward_varlen(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(cu_seqlens),
-                                      int(batch), int(num_heads_q), int(num_heads_kv),
-                                      int(max_seqlen_kv), int(head_dim), float(softmax_scale),
-                                      _stream_handle(stream))
+                            max_seqlen_kv, head_dim, softmax_scale=0.0, stream=None,
+                            kernel="auto") -> int:
+    """Raw C call of fmha_forward_varlen (kernel "auto") or
+    fmha_forward_varlen_variant ("chunk" or "ldg"); returns the status."""
+    args = (_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(cu_seqlens), int(batch), int(num_heads_q),
+            int(num_heads_kv), int(max_seqlen_kv), int(head_dim), float(softmax_scale))
+    if kernel == "auto":
+        return load().fmha_forward_varlen(*args, _stream_handle(stream))
+    return load().fmha_forward_varlen_variant(*args, VARLEN_KERNELS[kernel],
+                                              _stream_handle(stream))
 
 
 def device_error() -> int:

@@ -26,6 +26,8 @@ SIGNATURES = {
     "fmha_forward": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "fmha_forward_variant": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "fmha_forward_varlen": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp]),
+    "fmha_forward_varlen_variant": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                                         ctypes.c_float, _i, _vp]),
     "fmha_forward_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "fmha_status_string": (ctypes.c_char_p, [_i]),
     "fmha_device_error": (_i, [ctypes.POINTER(_i)]),

@@ -37,7 +37,7 @@ def nvcc() -> str:
 
 
 def _headers():
-    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h", ".hpp"))]
     return hs + [os.path.join(ROOT, "include", "fmha.h")]
 
 

@@ -341,10 +341,12 @@ fmha_status_t fmha_forward_variant(const void* Q, const void* K, const void* V, 
                                      : launch_bulk(P, head_dim, smax, g, c.warps, dev, s);
 }
 
-fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, void* O,
-                                  const int32_t* cu_seqlens_kv, int batch, int num_heads_q,
-                                  int num_heads_kv, int max_seqlen_kv, int head_dim,
-                                  float softmax_scale, fmha_stream_t stream) {
+fmha_status_t fmha_forward_varlen_variant(const void* Q, const void* K, const void* V,
+                                          void* O, const int32_t* cu_seqlens_kv, int batch,
+                                          int num_heads_q, int num_heads_kv, int max_seqlen_kv,
+                                          int head_dim, float softmax_scale, int variant,
+                                          fmha_stream_t stream) {
+  if (variant < FMHA_VARIANT_AUTO || variant > FMHA_VARIANT_LDG) return FMHA_ERR_INVALID_ARG;
   fmha_status_t st =
       check_args(Q, K, V, O, batch, num_heads_q, num_heads_kv, max_seqlen_kv, head_dim);
   if (st != FMHA_OK) return st;
@@ -376,12 +378,15 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
                                             : 1.0 / std::sqrt((double)head_dim);
   P.scale_log2 = (float)(1.4426950408889634 * scale);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  // Default: the chunk ring for both head_dims (on the reference's Poisson(4)
+  // AUTO: the chunk ring for both head_dims (on the reference's Poisson(4)
   // table it beats the register-prefetch kernel by 4-27 % at D=256 once its
-  // scores run on the tensor cores). FMHA_VARLEN_KERNEL=ldg|chunk overrides.
-  static const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
-  const bool use_ldg = (kind && *kind) ? std::strcmp(kind, "ldg") == 0 : false;
-  if (use_ldg) {
+  // scores run on the tensor cores). FMHA_VARLEN_KERNEL=ldg|chunk, read on
+  // every AUTO call, overrides that default.
+  if (variant == FMHA_VARIANT_AUTO) {
+    const char* kind = std::getenv("FMHA_VARLEN_KERNEL");
+    variant = (kind && std::strcmp(kind, "ldg") == 0) ? FMHA_VARIANT_LDG : FMHA_VARIANT_BULK;
+  }
+  if (variant == FMHA_VARIANT_LDG) {
     int bps = 1;
     st = blocks_per_sm(reinterpret_cast<const void*>(fn), kLdgThreads, &bps);
     if (st != FMHA_OK) return st;
@@ -421,6 +426,15 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, v
   const int grid = batch < dev.sms ? batch : dev.sms;
   cfn<<<grid, 32 * (1 + ncw), P.ring_off + ring, cs>>>(P);
   return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+}
+
+fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, void* O,
+                                  const int32_t* cu_seqlens_kv, int batch, int num_heads_q,
+                                  int num_heads_kv, int max_seqlen_kv, int head_dim,
+                                  float softmax_scale, fmha_stream_t stream) {
+  return fmha_forward_varlen_variant(Q, K, V, O, cu_seqlens_kv, batch, num_heads_q, num_heads_kv,
+                                     max_seqlen_kv, head_dim, softmax_scale, FMHA_VARIANT_AUTO,
+                                     stream);
 }
 
 fmha_status_t fmha_forward_append(const void* Q, void* K_cache, void* V_cache,
@@ -514,11 +528,17 @@ fmha_status_t fmha_seqlens_poisson(int batch, int max_seqlen_kv, uint32_t seed, 
                                    int32_t* out) {
   if (batch < 0 || max_seqlen_kv < 2 || !(lambda > 0.0) || (batch > 0 && !out))
     return FMHA_ERR_INVALID_ARG;
+  // A lambda far outside [2, max_seqlen_kv] would make the redraw loop run
+  // practically forever; the loop is capped and such a lambda is rejected.
+  if (!(lambda <= 4.0 * max_seqlen_kv + 64.0)) return FMHA_ERR_INVALID_ARG;
   std::mt19937 gen(seed);
   std::poisson_distribution<int> dist(lambda);
+  const long kMaxDraws = 1L << 20;  // per row
   for (int i = 0; i < batch; ++i) {
     int len;
+    long draws = 0;
     do {
+      if (++draws > kMaxDraws) return FMHA_ERR_INVALID_ARG;
       len = dist(gen);
     } while (len < 2 || len > max_seqlen_kv);
     out[i] = len;

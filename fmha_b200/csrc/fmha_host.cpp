@@ -42,6 +42,7 @@
 #include <vector>
 
 #include "fmha.h"
+#include "host_wait.hpp"
 
 namespace {
 
@@ -235,27 +236,31 @@ struct ShardResult {
   } while (0)
 
 // Waits for an event by polling with a deadline instead of blocking forever.
-bool wait_event(cudaEvent_t e, double timeout_s, std::string* why) {
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {
-    const cudaError_t q = cudaEventQuery(e);
-    if (q == cudaSuccess) return true;
-    if (q != cudaErrorNotReady) {
-      *why = std::string("cudaEventQuery: ") + cudaGetErrorString(q);
-      return false;
-    }
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
-      *why = "timed out waiting for the shard's kernels";
-      return false;
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
-  }
+// FMHA_HOST_STUCK_SHARD=g (test hook) makes shard g's query report "not
+// ready" for ever, with a 2 s deadline, so the timeout path runs without any
+// stuck device work.
+fmha_host::WaitOutcome wait_event(cudaEvent_t e, double timeout_s, bool stub_stuck,
+                                  std::string* why) {
+  if (stub_stuck) timeout_s = 2.0;
+  return fmha_host::wait_deadline(
+      [&] { return stub_stuck ? (int)cudaErrorNotReady : (int)cudaEventQuery(e); },
+      (int)cudaSuccess, (int)cudaErrorNotReady,
+      [](int c) { return std::string("cudaEventQuery: ") + cudaGetErrorString((cudaError_t)c); },
+      timeout_s, why);
 }
 
-int injected_failure_shard() {
-  const char* v = std::getenv("FMHA_HOST_FAIL_SHARD");
+struct CudaReleaseOps {
+  void free_buffer(void* p) { cudaFree(p); }
+  void destroy_stream(void* s) { cudaStreamDestroy(static_cast<cudaStream_t>(s)); }
+  void destroy_event(void* e) { cudaEventDestroy(static_cast<cudaEvent_t>(e)); }
+};
+
+int env_shard(const char* name) {
+  const char* v = std::getenv(name);
   return (v && *v) ? std::atoi(v) : -1;
 }
+
+int injected_failure_shard() { return env_shard("FMHA_HOST_FAIL_SHARD"); }
 
 // cu: global cu_seqlens (varlen mode) or empty.
 void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64_t rows,
@@ -268,17 +273,17 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
   void *dQ = nullptr, *dK = nullptr, *dV = nullptr, *dO = nullptr, *dCu = nullptr;
   cudaStream_t st = nullptr;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
-  bool started = false;  // passed the start line
+  bool started = false;    // passed the start line
+  bool in_flight = false;  // a wait gave up with this shard's kernels possibly running
   auto cleanup = [&] {
     if (!started) bar.drop();
-    if (e0) cudaEventDestroy(e0);
-    if (e1) cudaEventDestroy(e1);
-    if (st) cudaStreamDestroy(st);
-    cudaFree(dQ);
-    cudaFree(dK);
-    cudaFree(dV);
-    cudaFree(dO);
-    if (dCu) cudaFree(dCu);
+    fmha_host::ShardHandles h;
+    h.buffers[0] = dQ, h.buffers[1] = dK, h.buffers[2] = dV, h.buffers[3] = dO;
+    h.buffers[4] = dCu;
+    h.stream = st;
+    h.events[0] = e0, h.events[1] = e1;
+    CudaReleaseOps ops;
+    fmha_host::release_shard(h, in_flight, ops);
   };
   if (gpu == injected_failure_shard()) {  // host-side fault injection (no GPU fault)
     res.error = "injected failure (FMHA_HOST_FAIL_SHARD)";
@@ -319,7 +324,10 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
   SHARD_CUDA(cudaEventRecord(e0, st));
   for (int i = 0; i < o.iters; ++i) launch();
   SHARD_CUDA(cudaEventRecord(e1, st));
-  if (!wait_event(e1, 120.0, &res.error)) {
+  const fmha_host::WaitOutcome w =
+      wait_event(e1, 120.0, gpu == env_shard("FMHA_HOST_STUCK_SHARD"), &res.error);
+  if (w != fmha_host::WaitOutcome::kDone) {
+    in_flight = w == fmha_host::WaitOutcome::kTimedOut;
     cleanup();
     return;
   }

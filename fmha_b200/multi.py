@@ -46,6 +46,11 @@ def gather_output(local_o, shard: Shard, group=None):
     sizes = [torch.zeros_like(n) for _ in range(shard.world)]
     dist.all_gather(sizes, n, group=group)
     m = int(max(int(s.item()) for s in sizes))
+    if all(int(s.item()) == m for s in sizes):
+        # Equal shards: one collective straight into the output buffer.
+        out = torch.empty(m * shard.world, dtype=torch.uint8, device=raw.device)
+        dist.all_gather_into_tensor(out, raw.contiguous(), group=group)
+        return out.view(local_o.dtype)
     buf = torch.zeros(m, dtype=torch.uint8, device=raw.device)
     buf[:raw.numel()] = raw
     parts = [torch.empty_like(buf) for _ in range(shard.world)]

@@ -94,8 +94,9 @@ fmha_status_t fmha_forward_variant(const void* Q, const void* K, const void* V,
  *   cu_seqlens_kv [batch + 1] int32, device memory, cu[0] = 0, non-decreasing.
  * Each row length cu[b+1]-cu[b] must lie in 0..max_seqlen_kv (max_seqlen_kv
  * in 1..16); a longer row is skipped and reported through fmha_device_error
- * (FMHA_ERR_INVALID_ARG), an empty row yields zeros. softmax_scale <= 0 means
- * 1/sqrt(head_dim). Same grouping kvh = h / (Hq/Hkv) as fmha_forward.
+ * (FMHA_ERR_INVALID_ARG), an empty row yields zeros. softmax_scale == 0 means
+ * 1/sqrt(head_dim); a negative, NaN or infinite scale is rejected with
+ * FMHA_ERR_INVALID_ARG. Same grouping kvh = h / (Hq/Hkv) as fmha_forward.
  * Replaces launch_fmha_mfma_4x4x4 with its own argument list
  * (fmha_mfma_4x4x4_kernel.hpp:370-389; the layout of fmha_host.cpp:143-157).
  */
@@ -104,6 +105,20 @@ fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V,
                                   int batch, int num_heads_q, int num_heads_kv,
                                   int max_seqlen_kv, int head_dim,
                                   float softmax_scale, fmha_stream_t stream);
+
+/* fmha_forward_varlen with an explicit kernel: FMHA_VARIANT_BULK runs the
+ * chunk ring (whole packed rows staged by cp.async.bulk into a shared-memory
+ * byte ring), FMHA_VARIANT_LDG the register-prefetch kernel (persistent warps,
+ * 16-byte vector loads), FMHA_VARIANT_AUTO the default (the chunk ring, unless
+ * the environment variable FMHA_VARLEN_KERNEL=ldg is set when the call is
+ * made). Same reference counterpart as fmha_forward_varlen. */
+fmha_status_t fmha_forward_varlen_variant(const void* Q, const void* K,
+                                          const void* V, void* O,
+                                          const int32_t* cu_seqlens_kv,
+                                          int batch, int num_heads_q,
+                                          int num_heads_kv, int max_seqlen_kv,
+                                          int head_dim, float softmax_scale,
+                                          int variant, fmha_stream_t stream);
 
 /*
  * fmha_forward_append -- one decode step with a KV cache: writes this step's
@@ -162,8 +177,9 @@ fmha_status_t fmha_seqlens_poisson(int batch, int max_seqlen_kv, uint32_t seed,
                                    double lambda, int32_t* out);
 
 /* Test hook for the device-side failure path: while `on` is non-zero every
- * fmha_forward* call runs the bulk kernel with its producer issuing no
- * copies and a 20 ms wait bound, so each consumer's bounded wait runs out,
+ * fmha_forward / fmha_forward_variant call runs the dense bulk kernel with
+ * its producer issuing no copies (the varlen and append entry points ignore
+ * the hook) and a 20 ms wait bound, so each consumer's bounded wait runs out,
  * the kernel records FMHA_ERR_DEVICE_TIMEOUT in the device error word and
  * returns without trapping (output is left unwritten). No reference
  * counterpart. */

@@ -155,3 +155,41 @@ def test_append_rejects_bad_new_rows():
     assert lib.fmha_forward_append(*args) == _lib.FMHA_ERR_INVALID_ARG
     args[3] = 72
     assert lib.fmha_forward_append(*args) == _lib.FMHA_ERR_MISALIGNED
+
+
+@pytest.mark.parametrize("variant,status", [(7, _lib.FMHA_ERR_INVALID_ARG),
+                                            (-1, _lib.FMHA_ERR_INVALID_ARG)])
+def test_varlen_variant_rejects_unknown_kernel(variant, status):
+    lib = fmha_b200.load()
+    assert lib.fmha_forward_varlen_variant(16, 32, 48, 64, 80, 4, 16, 16, 16, 128, 0.0, variant,
+                                           None) == status
+    # the selector is checked before anything else, even for an empty batch
+    assert lib.fmha_forward_varlen_variant(None, None, None, None, None, 0, 16, 16, 16, 128, 0.0,
+                                           variant, None) == status
+
+
+def test_varlen_negative_scale_is_rejected_not_defaulted():
+    """softmax_scale == 0 selects 1/sqrt(head_dim); any negative value is an
+    error, never silently the default."""
+    for sc in (-1.0, -1e-30, float("-inf"), float("inf")):
+        assert varlen(scale=sc) == _lib.FMHA_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("lam,max_s", [(1000.0, 16), (200.0, 16), (1e6, 2)])
+def test_seqlens_poisson_rejects_lambda_far_from_range(lam, max_s):
+    """A lambda whose draws practically never land in [2, max_seqlen_kv]
+    returns FMHA_ERR_INVALID_ARG instead of looping for ever."""
+    out = np.empty(64, dtype=np.int32)
+    st = fmha_b200.load().fmha_seqlens_poisson(64, max_s, 42, lam, out.ctypes.data)
+    assert st == _lib.FMHA_ERR_INVALID_ARG
+
+
+def test_seqlens_poisson_redraw_cap_ends_the_loop():
+    """lambda inside the accepted range but with almost no mass in [2, 3]:
+    the per-row redraw cap ends the call with an error, in bounded time."""
+    import time
+    out = np.empty(4, dtype=np.int32)
+    t0 = time.perf_counter()
+    st = fmha_b200.load().fmha_seqlens_poisson(4, 3, 42, 60.0, out.ctypes.data)
+    assert st == _lib.FMHA_ERR_INVALID_ARG
+    assert time.perf_counter() - t0 < 30

@@ -40,3 +40,15 @@ def test_fmha_host_reports_a_failed_shard(cuda):
     assert "shard on GPU 0 failed: injected failure" in r.stderr
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert not line["passed"] and line["failed_shards"].startswith("0: injected failure")
+
+
+def test_fmha_host_stuck_shard_returns_without_blocking(cuda):
+    """The timed wait of shard 0 sees an event query stub that never
+    completes (FMHA_HOST_STUCK_SHARD, a host-side hook: no kernel is stuck).
+    After its 2 s deadline the shard reports the timeout and returns without
+    freeing its buffers, and the driver exits non-zero promptly."""
+    env = dict(os.environ, FMHA_HOST_STUCK_SHARD="0")
+    r = subprocess.run([BIN, "0", "--json", "--iters", "3"], capture_output=True, text=True,
+                       timeout=300, env=env)
+    assert r.returncode != 0
+    assert "shard on GPU 0 failed: timed out" in r.stderr

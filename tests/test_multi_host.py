@@ -33,15 +33,15 @@ def _free_port():
     return port
 
 
-SHAPE = (13, 32, 16, 5, 128)  # batch, hq, hkv, s, d
+SHAPE = (13, 32, 16, 5, 128)  # batch, hq, hkv, s, d (ragged shards: 7 + 6 rows)
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, shape=SHAPE):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from fmha_b200.multi import gather_output
     from oracle import oracle as O
-    b, hq, hkv, s, d = SHAPE
+    b, hq, hkv, s, d = shape
     sh = make_shard(b, hq, hkv, s, d, world, rank)
     q, k, v = O.make_inputs_bhsd(sh.rows, hq, hkv, s, d, seed=9, batch_offset=sh.row0)
     _, o16 = O.decode_bhsd(q, k, v, sh.rows, hq, hkv, s, d, want_f32=False)
@@ -53,10 +53,13 @@ def _worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def test_gloo_two_rank_shards_equal_single_process(tmp_path, oracle):
+@pytest.mark.parametrize("shape", [SHAPE, (12, 16, 16, 3, 128)], ids=["ragged", "equal"])
+def test_gloo_two_rank_shards_equal_single_process(tmp_path, oracle, shape):
+    """Ragged shards take the padded all-gather, equal shards the single
+    all_gather_into_tensor; both must give the 1-process output."""
     world = 2
-    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
-    b, hq, hkv, s, d = SHAPE
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), shape), nprocs=world, join=True)
+    b, hq, hkv, s, d = shape
     q, k, v = oracle.make_inputs_bhsd(b, hq, hkv, s, d, seed=9)
     _, ref = oracle.decode_bhsd(q, k, v, b, hq, hkv, s, d, want_f32=False)
     for r in range(world):

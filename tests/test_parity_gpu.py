@@ -51,6 +51,22 @@ def check_close(o_bits, ref32):
     return float(err.max())
 
 
+def check_all_rows(cuda, oracle, Q, K, V, O, B, hq, hkv, s, d, slice_rows=2048):
+    """Every row of a device-resident call against the oracle on the same
+    (device-generated) inputs, copied back slice by slice to bound host
+    memory. Returns the max abs error."""
+    oracle.set_threads(os.cpu_count() or 1)
+    bits = lambda x: x.cpu().view(cuda.int16).numpy().view(np.uint16)  # noqa: E731
+    qn, kn = hq * d, hkv * s * d
+    worst = 0.0
+    for r0 in range(0, B, slice_rows):
+        r1 = min(B, r0 + slice_rows)
+        ref32, _ = oracle.decode_bhsd(bits(Q[r0 * qn:r1 * qn]), bits(K[r0 * kn:r1 * kn]),
+                                      bits(V[r0 * kn:r1 * kn]), r1 - r0, hq, hkv, s, d)
+        worst = max(worst, check_close(bits(O[r0 * qn:r1 * qn]), ref32))
+    return worst
+
+
 SHAPES = []
 for d in (128, 256):
     for s in range(1, 17):
@@ -152,7 +168,7 @@ def test_device_timeout_is_reported_not_trapped(cuda, oracle):
 @pytest.mark.parametrize("hq,hkv,s,d", [(32, 32, 16, 256), (16, 16, 1, 128), (32, 16, 16, 256),
                                         (16, 16, 16, 128)])
 def test_full_size_properties(cuda, oracle, hq, hkv, s, d):
-    """batch 30720: sampled rows against the oracle,
+    """batch 30720: every row against the oracle,
     batch-shard invariance (two half-batch calls give the full call's bits),
     and determinism. Inputs are generated on the device."""
     B = 30720
@@ -172,13 +188,12 @@ def test_full_size_properties(cuda, oracle, hq, hkv, s, d):
     cuda.cuda.synchronize()
     assert fmha_b200.device_error() == 0
     assert cuda.equal(O.view(cuda.int16), O2.view(cuda.int16))
-    rows = np.unique(np.concatenate([np.random.default_rng(0).integers(0, B, 24), [0, B - 1]]))
-    for b0 in rows:
-        q, k, v = oracle.make_inputs_bhsd(1, hq, hkv, s, d, seed=0, batch_offset=int(b0))
-        ref32, _ = oracle.decode_bhsd(q, k, v, 1, hq, hkv, s, d)
-        got = O[b0 * hq * d:(b0 + 1) * hq * d].cpu().view(cuda.int16).numpy().view(np.uint16)
-        check_close(got, ref32)
-    del Q, K, V, O, O2
+    del O2
+    # The device generator is pinned to the host one elsewhere; spot-check it here.
+    q, _, _ = oracle.make_inputs_bhsd(1, hq, hkv, s, d, seed=0, batch_offset=B - 1)
+    assert np.array_equal(Q[(B - 1) * hq * d:].cpu().view(cuda.int16).numpy().view(np.uint16), q)
+    check_all_rows(cuda, oracle, Q, K, V, O, B, hq, hkv, s, d)
+    del Q, K, V, O
     cuda.cuda.empty_cache()
 
 
@@ -188,10 +203,10 @@ SWEEP = [(h, h, s, d) for s in (1, 2, 4, 8, 16) for d in (128, 256) for h in (16
 
 @pytest.mark.slow
 @pytest.mark.parametrize("hq,hkv,s,d", SWEEP, ids=str)
-def test_full_size_sweep_sampled(cuda, oracle, hq, hkv, s, d):
+def test_full_size_sweep_all_rows(cuda, oracle, hq, hkv, s, d):
     """Every BASELINE sweep shape (S x D x H, plus GQA 32/16 over S) at
-    batch 30720 through fmha_forward (AUTO family): 12 sampled rows, the
-    first and the last, against the oracle at the library tolerance."""
+    batch 30720 through fmha_forward (AUTO family): all 30720 rows against
+    the oracle at the library tolerance."""
     B = 30720
     Q = cuda.empty(B * hq * d, dtype=cuda.bfloat16, device="cuda")
     K = cuda.empty(B * hkv * s * d, dtype=cuda.bfloat16, device="cuda")
@@ -202,12 +217,6 @@ def test_full_size_sweep_sampled(cuda, oracle, hq, hkv, s, d):
     assert fmha_b200.fmha_forward_ptr(Q, K, V, O, B, hq, hkv, s, d) == 0
     cuda.cuda.synchronize()
     assert fmha_b200.device_error() == 0
-    rows = np.unique(np.concatenate([np.random.default_rng(s * d + hq).integers(0, B, 10),
-                                     [0, B - 1]]))
-    for b0 in rows:
-        q, k, v = oracle.make_inputs_bhsd(1, hq, hkv, s, d, seed=7, batch_offset=int(b0))
-        ref32, _ = oracle.decode_bhsd(q, k, v, 1, hq, hkv, s, d)
-        got = O[b0 * hq * d:(b0 + 1) * hq * d].cpu().view(cuda.int16).numpy().view(np.uint16)
-        check_close(got, ref32)
+    check_all_rows(cuda, oracle, Q, K, V, O, B, hq, hkv, s, d)
     del Q, K, V, O
     cuda.cuda.empty_cache()

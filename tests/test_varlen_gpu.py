@@ -1,7 +1,9 @@
 """fmha_forward_varlen (the reference's packed K/V layout [sum S_b, Hkv, D] +
 cu_seqlens_kv, fmha_host.cpp:143-157) against the oracle's packed-layout
 restatement, the reference's own golden output and its Poisson(4) seqlens
-(fmha_host.cpp:58-72)."""
+(fmha_host.cpp:58-72). Every parity test runs both varlen kernels, selected
+per call through fmha_forward_varlen_variant: the chunk ring (the default) and
+the register-prefetch kernel."""
 import glob
 import os
 
@@ -12,6 +14,8 @@ import fmha_b200
 from tests.test_parity_gpu import GUARD, POISON, check_close, to_dev
 
 pytestmark = pytest.mark.gpu
+
+KERNELS = ["chunk", "ldg"]
 
 
 def seqlens(oracle, b, kind, rng):
@@ -26,16 +30,15 @@ def seqlens(oracle, b, kind, rng):
     return np.full(b, int(kind), dtype=np.int32)
 
 
-def run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, max_s=16, scale=0.0):
+def run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, max_s=16, scale=0.0, kernel="chunk"):
     cu = np.concatenate([[0], np.cumsum(sl)]).astype(np.int32)
     n = b * hq * d
     Q, K, V = to_dev(cuda, q), to_dev(cuda, k), to_dev(cuda, v)
     CU = cuda.from_numpy(cu).cuda()
     buf = cuda.full((n + 2 * GUARD,), POISON, dtype=cuda.int16, device="cuda")
     O = buf[GUARD:GUARD + n]
-    lib = fmha_b200.load()
-    st = lib.fmha_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
-                                 CU.data_ptr(), b, hq, hkv, max_s, d, scale, None)
+    st = fmha_b200.fmha_forward_varlen_ptr(Q, K, V, O, CU, b, hq, hkv, max_s, d, scale, 0,
+                                           kernel=kernel)
     assert st == 0, fmha_b200.status_string(st)
     cuda.cuda.synchronize()
     err = fmha_b200.device_error()
@@ -49,15 +52,16 @@ CASES = [(b, hq, hkv, d, kind) for d in (128, 256) for (b, hq, hkv) in ((37, 16,
          for kind in ("poisson", "edge", "1", "3", "16")]
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("b,hq,hkv,d,kind", CASES, ids=str)
-def test_varlen_vs_oracle(cuda, oracle, b, hq, hkv, d, kind):
+def test_varlen_vs_oracle(cuda, oracle, b, hq, hkv, d, kind, kernel):
     rng = np.random.default_rng(b * 7 + d)
     sl = seqlens(oracle, b, kind, rng)
     t = int(sl.sum())
     q = oracle.gen_bf16(b * hq * d, 31, 1)
     k = oracle.gen_bf16(t * hkv * d, 31, 2)
     v = oracle.gen_bf16(t * hkv * d, 31, 3)
-    out, err, cu = run_varlen(cuda, q, k, v, sl, b, hq, hkv, d)
+    out, err, cu = run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, kernel=kernel)
     assert err == 0
     ref32, _ = oracle.decode_thd(q, k, v, cu, b, hq, hkv, d)
     check_close(out, ref32)
@@ -66,8 +70,9 @@ def test_varlen_vs_oracle(cuda, oracle, b, hq, hkv, d, kind):
 GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "thd_*.npz")))
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("path", GOLDEN, ids=os.path.basename)
-def test_varlen_vs_reference_golden(cuda, oracle, path):
+def test_varlen_vs_reference_golden(cuda, oracle, path, kernel):
     """The reference's own output on its own layout and seqlens, under its
     own tolerance (fmha_host.cpp:260)."""
     f = np.load(path)
@@ -77,18 +82,20 @@ def test_varlen_vs_reference_golden(cuda, oracle, path):
     q = oracle.gen_bf16(b * h * d, seed, 1)
     k = oracle.gen_bf16(t * h * d, seed, 2)
     v = oracle.gen_bf16(t * h * d, seed, 3)
-    out, err, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d)
+    out, err, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, kernel=kernel)
     assert err == 0
     o = out.view(np.float16).astype(np.float32)
     r = f["ref_o"].view(np.float16).astype(np.float32)
     assert np.all(np.abs(o - r) <= 1e-2 + 1e-2 * np.abs(r))
 
 
-def test_varlen_uniform_matches_dense(cuda, oracle):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_varlen_uniform_matches_dense(cuda, oracle, kernel):
     b, h, s, d = 64, 16, 5, 256
     q, k, v = oracle.make_inputs_bhsd(b, h, h, s, d, seed=8)
     packed = lambda x: np.ascontiguousarray(x.reshape(b, h, s, d).transpose(0, 2, 1, 3)).reshape(-1)  # noqa
-    out, err, _ = run_varlen(cuda, q, packed(k), packed(v), np.full(b, s, np.int32), b, h, h, d)
+    out, err, _ = run_varlen(cuda, q, packed(k), packed(v), np.full(b, s, np.int32), b, h, h, d,
+                             kernel=kernel)
     assert err == 0
     from tests.test_parity_gpu import run_kernel
     dense = run_kernel(cuda, q, k, v, b, h, h, s, d)
@@ -97,20 +104,22 @@ def test_varlen_uniform_matches_dense(cuda, oracle):
     assert np.abs(a - c).max() <= 2e-3
 
 
-def test_varlen_explicit_scale(cuda, oracle):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_varlen_explicit_scale(cuda, oracle, kernel):
     b, h, d = 5, 16, 128
     sl = np.array([4, 4, 4, 4, 4], np.int32)
     q = oracle.gen_bf16(b * h * d, 3, 1)
     k = oracle.gen_bf16(20 * h * d, 3, 2)
     v = oracle.gen_bf16(20 * h * d, 3, 3)
-    a, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=0.0)
-    c, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=1.0 / np.sqrt(d))
+    a, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=0.0, kernel=kernel)
+    c, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=1.0 / np.sqrt(d), kernel=kernel)
     assert np.array_equal(a, c)
-    e, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=0.5)
+    e, _, _ = run_varlen(cuda, q, k, v, sl, b, h, h, d, scale=0.5, kernel=kernel)
     assert not np.array_equal(a, e)
 
 
-def test_varlen_rejects_long_row_on_device(cuda, oracle):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_varlen_rejects_long_row_on_device(cuda, oracle, kernel):
     """A row longer than max_seqlen_kv is skipped and flagged in the device
     error word; the other rows are still computed."""
     b, h, d = 4, 16, 128
@@ -119,7 +128,7 @@ def test_varlen_rejects_long_row_on_device(cuda, oracle):
     q = oracle.gen_bf16(b * h * d, 4, 1)
     k = oracle.gen_bf16(t * h * d, 4, 2)
     v = oracle.gen_bf16(t * h * d, 4, 3)
-    out, err, cu = run_varlen(cuda, q, k, v, sl, b, h, h, d, max_s=8)
+    out, err, cu = run_varlen(cuda, q, k, v, sl, b, h, h, d, max_s=8, kernel=kernel)
     assert err & 0xff == fmha_b200.FMHA_ERR_INVALID_ARG and (err >> 8) == 5
     ref32, _ = oracle.decode_thd(q, k, v, cu, b, h, h, d)
     n = h * d
@@ -129,10 +138,11 @@ def test_varlen_rejects_long_row_on_device(cuda, oracle):
 
 
 @pytest.mark.slow
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("hq,d", [(16, 128), (32, 256)])
-def test_varlen_full_size_reference_seqlens(cuda, oracle, hq, d):
-    """batch 30720 with the reference's own Poisson seqlens: sampled rows vs
-    the oracle, generated on the device."""
+def test_varlen_full_size_reference_seqlens(cuda, oracle, hq, d, kernel):
+    """batch 30720 with the reference's own Poisson seqlens, inputs generated
+    on the device: every row against the oracle."""
     B = 30720
     sl = seqlens(oracle, B, "poisson", np.random.default_rng(0))
     cu = np.concatenate([[0], np.cumsum(sl)]).astype(np.int32)
@@ -144,19 +154,14 @@ def test_varlen_full_size_reference_seqlens(cuda, oracle, hq, d):
         fmha_b200.fill_normal_bf16(x, seed=0, tensor_id=tid)
     O = cuda.empty(B * hq * d, dtype=cuda.float16, device="cuda")
     CU = cuda.from_numpy(cu).cuda()
-    lib = fmha_b200.load()
-    assert lib.fmha_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
-                                   CU.data_ptr(), B, hq, hq, 16, d, 0.0, None) == 0
+    assert fmha_b200.fmha_forward_varlen_ptr(Q, K, V, O, CU, B, hq, hq, 16, d, 0.0, 0,
+                                             kernel=kernel) == 0
     cuda.cuda.synchronize()
     assert fmha_b200.device_error() == 0
-    for b0 in (0, 1, 12345, B - 1):
-        s = int(sl[b0])
-        q = oracle.gen_bf16(hq * d, 0, 1, b0 * hq * d)
-        k = oracle.gen_bf16(s * hq * d, 0, 2, int(cu[b0]) * hq * d)
-        v = oracle.gen_bf16(s * hq * d, 0, 3, int(cu[b0]) * hq * d)
-        ref32, _ = oracle.decode_thd(q, k, v, np.array([0, s], np.int32), 1, hq, hq, d)
-        got = O[b0 * hq * d:(b0 + 1) * hq * d].cpu().view(cuda.int16).numpy().view(np.uint16)
-        check_close(got, ref32)
+    oracle.set_threads(os.cpu_count() or 1)
+    bits = lambda x: x.cpu().view(cuda.int16).numpy().view(np.uint16)  # noqa: E731
+    ref32, _ = oracle.decode_thd(bits(Q), bits(K), bits(V), cu, B, hq, hq, d)
+    check_close(bits(O), ref32)
 
 
 PLAN_CASES = [  # (hq, hkv, d, chunk byte limit or 0 for the default, max_seqlen_kv)
@@ -169,8 +174,10 @@ PLAN_CASES = [  # (hq, hkv, d, chunk byte limit or 0 for the default, max_seqlen
 ]
 
 
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("hq,hkv,d,chunk,max_s", PLAN_CASES, ids=str)
-def test_varlen_chunk_planning_all_rows(cuda, oracle, monkeypatch, hq, hkv, d, chunk, max_s):
+def test_varlen_chunk_planning_all_rows(cuda, oracle, monkeypatch, hq, hkv, d, chunk, max_s,
+                                        kernel):
     """Enough rows that every CTA plans several 32-row windows, packs rows into
     chunks and wraps its ring many times; lengths mix Poisson(4) with 0, 1,
     16 and (when max_seqlen_kv < 16) rows that must be flagged and skipped.
@@ -187,7 +194,7 @@ def test_varlen_chunk_planning_all_rows(cuda, oracle, monkeypatch, hq, hkv, d, c
     q = oracle.gen_bf16(b * hq * d, 77, 1)
     k = oracle.gen_bf16(t * hkv * d, 77, 2)
     v = oracle.gen_bf16(t * hkv * d, 77, 3)
-    out, err, cu = run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, max_s=max_s)
+    out, err, cu = run_varlen(cuda, q, k, v, sl, b, hq, hkv, d, max_s=max_s, kernel=kernel)
     bad = sl > max_s
     if bad.any():
         assert err & 0xff == fmha_b200.FMHA_ERR_INVALID_ARG and (err >> 8) == 5
@@ -200,7 +207,8 @@ def test_varlen_chunk_planning_all_rows(cuda, oracle, monkeypatch, hq, hkv, d, c
     assert np.all(out[~rows_ok] == POISON)
 
 
-def test_varlen_negative_lengths_cover_every_valid_row(cuda, oracle):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_varlen_negative_lengths_cover_every_valid_row(cuda, oracle, kernel):
     """cu_seqlens that is not monotonic (a few negative lengths) makes the
     byte-balanced CTA ranges irregular; every valid row must still be
     computed (no gaps), invalid rows flagged and left untouched."""
@@ -220,10 +228,8 @@ def test_varlen_negative_lengths_cover_every_valid_row(cuda, oracle):
     Q, K, V = to_dev(cuda, q), to_dev(cuda, k), to_dev(cuda, v)
     CU = cuda.from_numpy(cu).cuda()
     buf = cuda.full((n + 2 * GUARD,), POISON, dtype=cuda.int16, device="cuda")
-    lib = fmha_b200.load()
-    st = lib.fmha_forward_varlen(Q.data_ptr(), K.data_ptr(), V.data_ptr(),
-                                 buf[GUARD:GUARD + n].data_ptr(), CU.data_ptr(), b, hq, hkv, 16, d,
-                                 0.0, None)
+    st = fmha_b200.fmha_forward_varlen_ptr(Q, K, V, buf[GUARD:GUARD + n], CU, b, hq, hkv, 16, d,
+                                           0.0, 0, kernel=kernel)
     assert st == 0
     cuda.cuda.synchronize()
     err = fmha_b200.device_error()
