@@ -71,7 +71,90 @@ struct Params {
   const uint16_t* K_new;  // [units, D]: this step's K row of every unit
   const uint16_t* V_new;
   int64_t kv_ustride;     // elements between consecutive units' K slabs (cache stride)
+  // ldg family: dynamic tail (see sched_join). sched_tag == 0: fully static.
+  unsigned long long* sched;  // this launch's schedule word
+  uint32_t sched_tag;         // 24-bit launch tag, unique among launches in flight
+  int64_t sched_rounds;       // static rounds per warp before the dynamic tail
 };
+
+// ------------------------------------------------------------ launch overlap
+// Programmatic dependent launch (the host launches with the
+// programmatic-stream-serialization attribute): a kernel lets the next
+// kernel of its stream start launching right away, so that kernel's CTAs take
+// each SM as soon as this one's CTA leaves it instead of after the whole grid
+// and a launch gap; the next kernel in turn waits in grid_dependency_wait()
+// until this grid has completed and its writes are visible, before it touches
+// any memory an earlier kernel may write (inputs and outputs alike). Without
+// the attribute both are no-ops.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------ dynamic tail
+// A persistent kernel splits its steps into a static part (warp w takes steps
+// w, w+W, ... for `sched_rounds` rounds) and a tail that warps claim one step
+// at a time, so SMs that stream faster than others take more of the tail and
+// all finish together. Each launch uses one schedule slot in device memory
+// (a few static slots; the host hands a slot and a tag to each launch):
+//   word 0: tag (24 bits, bits 40..63) | users (12 bits, bits 28..39);
+//   kSchedLanes claim counters, each on its own 128-byte line: warp w of a
+//   CTA claims tail steps R*W + (w % kSchedLanes) + kSchedLanes*c from
+//   counter w % kSchedLanes (one counter for every warp would queue ~1200
+//   claimers on one address; measured ~4 ns per same-address atomic).
+// A slot is all zeros whenever no launch uses it: the last user clears the
+// counters and then the word, so no launch ever needs it cleared beforehand.
+// Joining and leaving are one atomicAdd each on the word (a CAS loop there,
+// with every CTA of the grid arriving at once, cost tens of microseconds):
+//  * join: add one user. The old word tells the rest: all zero -> this CTA
+//    is the first user and adds its launch's tag; its own tag -> joined; tag
+//    0 with users -> the first user is installing, wait (bounded) for its tag;
+//    a foreign tag -> leave again and run every step statically (w, w+W, ...).
+//  * leave: remove one user. The CTA that removes the last one clears the
+//    counters and then the tag (a CAS from "tag, no users" to 0, which fails
+//    harmlessly if someone joined meanwhile; that CTA clears it later).
+// Coverage: if any CTA joined, each counter runs until its steps pass the
+// end, so every tail step is computed; CTAs that did not join compute their
+// static share of the tail too (the same values, so writing them twice is
+// benign; the same holds for a CTA that joins after the others have cleared
+// the slot).
+constexpr unsigned long long kSchedUser = 1ull << 28;
+constexpr unsigned long long kSchedUserMask = 0xfffull << 28;
+constexpr int kSchedLanes = 8;
+constexpr int kSchedCtrStride = 16;                       // 64-bit words (128 bytes)
+constexpr int kSchedSlotWords = kSchedCtrStride * (kSchedLanes + 1);
+
+__device__ __forceinline__ unsigned long long* sched_counter(unsigned long long* slot, int j) {
+  return slot + kSchedCtrStride * (1 + j);
+}
+
+__device__ __forceinline__ void sched_leave(unsigned long long* w) {
+  const unsigned long long old = atomicAdd(w, 0ull - kSchedUser);
+  if ((old & kSchedUserMask) != kSchedUser) return;  // others still use the slot
+  for (int j = 0; j < kSchedLanes; ++j) atomicExch(sched_counter(w, j), 0ull);
+  __threadfence();
+  atomicCAS(w, old - kSchedUser, 0ull);
+}
+
+__device__ __forceinline__ bool sched_join(unsigned long long* w, uint32_t tag) {
+  if (!w || tag == 0) return false;
+  const unsigned long long mine = (unsigned long long)tag << 40;
+  unsigned long long old = atomicAdd(w, kSchedUser);
+  if (old == 0) {
+    atomicAdd(w, mine);  // first user: the tag field was 0
+    return true;
+  }
+  // Tag 0 with users: the first user has not added its tag yet.
+  for (int it = 0; (old >> 40) == 0 && it < 100000; ++it) {
+    __nanosleep(100);
+    old = atomicAdd(w, 0ull);
+  }
+  if ((old >> 40) == tag) return true;
+  sched_leave(w);  // foreign (or still untagged): do not use the slot
+  return false;
+}
 
 template <int D, int SMAX, int G>
 struct TileShape {

@@ -2,12 +2,14 @@
 // tiles' K/V rows straight into registers with 16-byte streaming loads
 // (ld.global.nc, no L1 allocation, 256-byte L2 fetch), then compute.
 //
-// Each warp takes TPI consecutive tiles per step (tiles t0 .. t0+TPI-1, t0
-// advancing by TPI * total warps) and issues every load of the step before
-// the first arithmetic, so each warp keeps TPI*NP*2 16-byte loads per lane in
-// flight. This is the register-resident counterpart of the bulk family and is
-// kept as the comparison point the dispatcher measures against.
-//
+// Each warp takes TPI consecutive tiles per step (tiles s*TPI .. s*TPI+TPI-1
+// of step s) and issues every load of the step before the first arithmetic,
+// so each warp keeps TPI*NP*2 16-byte loads per lane in flight. Steps are
+// dealt out statically (warp w: w, w+W, ...) for P.sched_rounds rounds; the
+// remaining tail is claimed one step at a time from the launch's schedule
+// slot (sched_join; warp w claims from counter w % kSchedLanes), each claim
+// issued one step ahead so its latency hides behind the current step. This evens out SMs that stream at different rates
+// (a static schedule left the slowest SM ~7 % behind the fastest).
 // Compiled once per head_dim: -DFMHA_HEAD_DIM=128 or 256.
 #include "decode_common.cuh"
 
@@ -34,10 +36,39 @@ __global__ void __launch_bounds__(kLdgThreads) decode_ldg_kernel(const Params P)
   const int ul = OutputMap<D, SMAX, G>::unit(lane);
   const int s_len = P.s_len;
   const int64_t tiles = (P.units + T::NU - 1) / T::NU;
+  const int64_t steps = (tiles + TPI - 1) / TPI;
   const int64_t gw = (int64_t)blockIdx.x * WPB + warp;
-  const int64_t stride = (int64_t)gridDim.x * WPB * TPI;
+  const int64_t W = (int64_t)gridDim.x * WPB;
+  const int64_t R = P.sched_rounds;
+  __shared__ int s_joined;
+  allow_dependent_launch();
+  // The schedule slot is this launch's own; everything else waits for the
+  // previous kernel of the stream.
+  if (threadIdx.x == 0) s_joined = sched_join(P.sched, P.sched_tag) ? 1 : 0;
+  grid_dependency_wait();
+  __syncthreads();
+  const bool dyn = s_joined != 0;
+  // Step of round r: static below R (or always when not joined), else claimed
+  // from this warp's counter: tail steps R*W + j + kSchedLanes*c.
+  const int j = warp % kSchedLanes;
+  unsigned long long* ctr = dyn ? sched_counter(P.sched, j) : nullptr;
+  auto tail_step = [&](unsigned long long c) {
+    return R * W + j + (int64_t)kSchedLanes * (int64_t)__shfl_sync(kFullMask, c, 0);
+  };
+  int64_t r = 0;
+  int64_t step = gw;
+  if (dyn && R == 0) {
+    unsigned long long tk = 0;
+    if (lane == 0) tk = atomicAdd(ctr, 1ull);
+    step = tail_step(tk);
+  }
 
-  for (int64_t t0 = gw * TPI; t0 < tiles; t0 += stride) {
+  while (step < steps) {
+    const int64_t t0 = step * TPI;
+    // Claim the next step now if it comes from the tail; used after this one.
+    const bool claim_next = dyn && r + 1 >= R;
+    unsigned long long tk = 0;
+    if (claim_next && lane == 0) tk = atomicAdd(ctr, 1ull);
     uint4 kr[TPI][T::NP], vr[TPI][T::NP], qr[TPI][G];
     int uv[TPI];
 #pragma unroll
@@ -85,7 +116,11 @@ __global__ void __launch_bounds__(kLdgThreads) decode_ldg_kernel(const Params P)
         for (int g = 0; g < G; ++g) stg_stream(orow + g * D, pack8_f16(acc[g]));
       }
     }
+    ++r;
+    step = claim_next ? tail_step(tk) : gw + r * W;
   }
+  __syncthreads();  // every warp of the CTA has made its last claim
+  if (dyn && threadIdx.x == 0) sched_leave(P.sched);
 }
 
 #define FMHA_CAT2(a, b) a##b

@@ -24,6 +24,14 @@ namespace fmha {
 
 __device__ unsigned int g_fmha_device_error;
 
+// Schedule words of the ldg family's dynamic tail (decode_common.cuh,
+// sched_join): one per slot, each 0 whenever no launch is using it. Launches
+// take slots round-robin, so launches in flight at the same time normally use
+// different words; one that finds its word held by another launch runs
+// statically.
+constexpr int kSchedSlots = 16;
+__device__ __align__(128) unsigned long long g_fmha_sched[kSchedSlots * kSchedSlotWords];
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -33,11 +41,13 @@ struct DeviceInfo {
   int sms = 0;
   int smem_optin = 0;
   unsigned int* err = nullptr;  // device address of g_fmha_device_error
+  unsigned long long* sched = nullptr;  // device address of g_fmha_sched
 };
 
 std::mutex g_mu;
 std::atomic<int> g_test_stall{0};
 DeviceInfo g_dev[kMaxDevices];
+std::atomic<uint64_t> g_launch_seq[kMaxDevices];
 std::set<std::pair<const void*, int>> g_smem_set;      // (kernel, device) with smem attr set
 struct OccEntry {
   const void* fn;
@@ -62,6 +72,8 @@ fmha_status_t device_info(DeviceInfo* out) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_fmha_device_error) != cudaSuccess) return FMHA_ERR_CUDA;
     d.err = static_cast<unsigned int*>(p);
+    if (cudaGetSymbolAddress(&p, g_fmha_sched) != cudaSuccess) return FMHA_ERR_CUDA;
+    d.sched = static_cast<unsigned long long*>(p);
     d.ready = true;
   }
   *out = d;
@@ -232,6 +244,62 @@ int ldg_tpi(int smax, int g) {
 #undef FMHA_T
 }
 
+// Launches a persistent kernel with programmatic stream serialization, so it
+// may begin launching while the previous kernel of the stream finishes (the
+// kernel waits in grid_dependency_wait before touching shared data).
+// FMHA_NO_PDL=1 launches it the plain way.
+template <class Prm>
+cudaError_t launch_overlapped(void (*fn)(const Prm), unsigned grid, unsigned block, size_t smem,
+                              cudaStream_t stream, const Prm& P) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = env_int("FMHA_NO_PDL", 0) ? 0 : 1;
+  return cudaLaunchKernelEx(&cfg, fn, P);
+}
+
+// Share of the steps dealt out statically; the rest is the dynamic tail.
+constexpr int kStaticPercent = 90;
+
+// Fills P's schedule fields for a persistent launch of `warps` warps over
+// `steps` steps: a slot and a fresh tag for eager launches, tag 0 (fully
+// static) while the stream is being captured into a CUDA graph (a captured
+// launch would replay one tag, and two replays must never share a tail) or
+// for grids beyond the 12-bit user count.
+void plan_schedule(Params& P, const DeviceInfo& dev, int64_t steps, int64_t warps,
+                   cudaStream_t stream) {
+  P.sched = nullptr;
+  P.sched_tag = 0;
+  P.sched_rounds = 0;
+  if (env_int("FMHA_STATIC_SCHEDULE", 0)) return;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  if (cap != cudaStreamCaptureStatusNone) return;
+  int pct = env_int("FMHA_STATIC_PERCENT", kStaticPercent);  // tuning knob, 0..100
+  if (pct < 0 || pct > 100) pct = kStaticPercent;
+  const int64_t rounds = steps * pct / 100 / warps;
+  if (warps >= 4096) return;  // 12-bit user count (one user per CTA, fewer CTAs than warps)
+  int dv = 0;
+  if (cudaGetDevice(&dv) != cudaSuccess) return;
+  // FMHA_SCHED_SLOTS (1..16) narrows the slot pool; tests use it to make
+  // concurrent launches contend for one word.
+  int nslots = env_int("FMHA_SCHED_SLOTS", kSchedSlots);
+  if (nslots < 1 || nslots > kSchedSlots) nslots = kSchedSlots;
+  const uint64_t seq = g_launch_seq[dv].fetch_add(1);
+  P.sched = dev.sched + (seq % (uint64_t)nslots) * kSchedSlotWords;
+  P.sched_tag = (uint32_t)(seq % 0xffffffu) + 1u;
+  P.sched_rounds = rounds;
+}
+
 fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev,
                          cudaStream_t stream, bool append = false) {
   KernelFn fn = append ? (d == 128 ? ldg_append_kernel_d128(smax, g)
@@ -250,8 +318,12 @@ fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev
   const int64_t need = (tiles + (int64_t)wpb * tpi - 1) / ((int64_t)wpb * tpi);
   int64_t grid = (int64_t)dev.sms * bps;
   if (grid > need) grid = need;
-  fn<<<(unsigned)grid, kLdgThreads, 0, stream>>>(P);
-  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+  plan_schedule(P, dev, (tiles + tpi - 1) / tpi, grid * wpb, stream);
+  if (launch_overlapped(fn, (unsigned)grid, kLdgThreads, 0, stream, P) != cudaSuccess) {
+    cudaGetLastError();
+    return FMHA_ERR_CUDA;
+  }
+  return FMHA_OK;
 }
 
 // splitmix64 finaliser (Steele, Lea, Flood, OOPSLA 2014).
