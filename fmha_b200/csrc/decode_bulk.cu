@@ -1,13 +1,14 @@
 // decode_bulk.cu -- "bulk" kernel family: persistent CTAs (one per SM) that
 // stream contiguous runs of units through a shared-memory ring with 1-D
-// cp.async.bulk copies completing on mbarriers, consumed by 8 compute warps.
+// cp.async.bulk copies completing on mbarriers, consumed by 8-16 compute
+// warps (the launch picks the count per shape).
 //
-// Per CTA: warp 0 lane 0 is the producer; warps 1..8 are consumers. The CTA
+// Per CTA: warp 0 lane 0 is the producer; the other warps consume. The CTA
 // owns chunks c = blockIdx.x + k*gridDim.x (k = 0, 1, ...); chunk c covers
 // units [c*CU, min((c+1)*CU, units)), i.e. three contiguous byte ranges (K
 // slabs, V slabs, Q rows), each moved by one bulk copy into ring stage
 // k % NS. A chunk holds CT tiles; consumer warp w takes flat jobs
-// f = w, w+8, ... (chunk f / CT, tile f % CT), waits for the stage's `full`
+// f = w, w+ncw, ... (chunk f / CT, tile f % CT), waits for the stage's `full`
 // phase, computes the tile from shared memory, arrives on the stage's `empty`
 // barrier (count CT) and streams its fp16 output rows straight to global.
 //
@@ -34,6 +35,7 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const P
   volatile int* issued_ctr = abort_flag + 1;  // chunks whose copies are armed
   const uint32_t ring0 = smem_u32(smem + P.ring_off);
 
+  allow_dependent_launch();
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(full0 + 8u * i, 1);
@@ -43,6 +45,8 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const P
     *issued_ctr = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // Inputs and outputs may be written by the previous kernel of the stream.
+  grid_dependency_wait();
   __syncthreads();
 
   const int my_chunks =

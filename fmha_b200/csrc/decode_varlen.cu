@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(kLdgThreads) decode_varlen_kernel(const Varlen
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   float* sc = sc_all[warp];
+  allow_dependent_launch();
+  grid_dependency_wait();  // inputs and outputs may be written by the previous kernel
   // Warps take work items round-robin: item = (batch row, head range of hpi
   // heads, ~4 by default).
   // A long row (one head per tile) is thereby spread over several warps

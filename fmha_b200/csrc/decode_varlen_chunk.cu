@@ -197,6 +197,7 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
   const uint32_t ring0 = smem_u32(ring);
   const uint32_t R = P.stage_bytes;  // ring size in bytes (a multiple of the row size D*2)
 
+  allow_dependent_launch();
   if (threadIdx.x == 0) {
     for (int i = 0; i < M; ++i) {
       mbar_init(full0 + 8u * i, 1);
@@ -209,6 +210,8 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1)
     *next_tile = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // Inputs and outputs may be written by the previous kernel of the stream.
+  grid_dependency_wait();
   __syncthreads();
 
 

@@ -176,6 +176,62 @@ fmha_status_t check_args(const void* Q, const void* K, const void* V, void* O, i
   return FMHA_OK;
 }
 
+// Launches a persistent kernel with programmatic stream serialization, so it
+// may begin launching while the previous kernel of the stream finishes (the
+// kernel waits in grid_dependency_wait before touching shared data).
+// FMHA_NO_PDL=1 launches it the plain way.
+template <class Prm>
+cudaError_t launch_overlapped(void (*fn)(const Prm), unsigned grid, unsigned block, size_t smem,
+                              cudaStream_t stream, const Prm& P) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = env_int("FMHA_NO_PDL", 0) ? 0 : 1;
+  return cudaLaunchKernelEx(&cfg, fn, P);
+}
+
+// Share of the steps dealt out statically; the rest is the dynamic tail.
+constexpr int kStaticPercent = 90;
+
+// Fills P's schedule fields for a persistent launch of `ctas` CTAs whose
+// `workers` (warps or producers) share `steps` steps: a slot and a fresh tag for eager launches, tag 0 (fully
+// static) while the stream is being captured into a CUDA graph (a captured
+// launch would replay one tag, and two replays must never share a tail) or
+// for grids beyond the 12-bit user count.
+void plan_schedule(Params& P, const DeviceInfo& dev, int64_t steps, int64_t workers,
+                   int64_t ctas, cudaStream_t stream) {
+  P.sched = nullptr;
+  P.sched_tag = 0;
+  P.sched_rounds = 0;
+  if (env_int("FMHA_STATIC_SCHEDULE", 0)) return;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  if (cap != cudaStreamCaptureStatusNone) return;
+  int pct = env_int("FMHA_STATIC_PERCENT", kStaticPercent);  // tuning knob, 0..100
+  if (pct < 0 || pct > 100) pct = kStaticPercent;
+  const int64_t rounds = steps * pct / 100 / workers;
+  if (ctas >= 4096) return;  // 12-bit user count (one user per CTA)
+  int dv = 0;
+  if (cudaGetDevice(&dv) != cudaSuccess) return;
+  // FMHA_SCHED_SLOTS (1..16) narrows the slot pool; tests use it to make
+  // concurrent launches contend for one word.
+  int nslots = env_int("FMHA_SCHED_SLOTS", kSchedSlots);
+  if (nslots < 1 || nslots > kSchedSlots) nslots = kSchedSlots;
+  const uint64_t seq = g_launch_seq[dv].fetch_add(1);
+  P.sched = dev.sched + (seq % (uint64_t)nslots) * kSchedSlotWords;
+  P.sched_tag = (uint32_t)(seq % 0xffffffu) + 1u;
+  P.sched_rounds = rounds;
+}
+
 fmha_status_t launch_bulk(Params P, int d, int smax, int g, int warps, const DeviceInfo& dev,
                           cudaStream_t stream) {
   KernelFn fn = d == 128 ? bulk_kernel_d128(smax, g) : bulk_kernel_d256(smax, g);
@@ -221,8 +277,11 @@ fmha_status_t launch_bulk(Params P, int d, int smax, int g, int warps, const Dev
   if (st != FMHA_OK) return st;
   int grid = dev.sms * ctas_per_sm;
   if (grid > P.chunks) grid = P.chunks;
-  fn<<<grid, 32 * (1 + ncw), smem, stream>>>(P);
-  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+  if (launch_overlapped(fn, (unsigned)grid, 32u * (1 + ncw), smem, stream, P) != cudaSuccess) {
+    cudaGetLastError();
+    return FMHA_ERR_CUDA;
+  }
+  return FMHA_OK;
 }
 
 template <int D>
@@ -244,62 +303,6 @@ int ldg_tpi(int smax, int g) {
 #undef FMHA_T
 }
 
-// Launches a persistent kernel with programmatic stream serialization, so it
-// may begin launching while the previous kernel of the stream finishes (the
-// kernel waits in grid_dependency_wait before touching shared data).
-// FMHA_NO_PDL=1 launches it the plain way.
-template <class Prm>
-cudaError_t launch_overlapped(void (*fn)(const Prm), unsigned grid, unsigned block, size_t smem,
-                              cudaStream_t stream, const Prm& P) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(block);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = env_int("FMHA_NO_PDL", 0) ? 0 : 1;
-  return cudaLaunchKernelEx(&cfg, fn, P);
-}
-
-// Share of the steps dealt out statically; the rest is the dynamic tail.
-constexpr int kStaticPercent = 90;
-
-// Fills P's schedule fields for a persistent launch of `warps` warps over
-// `steps` steps: a slot and a fresh tag for eager launches, tag 0 (fully
-// static) while the stream is being captured into a CUDA graph (a captured
-// launch would replay one tag, and two replays must never share a tail) or
-// for grids beyond the 12-bit user count.
-void plan_schedule(Params& P, const DeviceInfo& dev, int64_t steps, int64_t warps,
-                   cudaStream_t stream) {
-  P.sched = nullptr;
-  P.sched_tag = 0;
-  P.sched_rounds = 0;
-  if (env_int("FMHA_STATIC_SCHEDULE", 0)) return;
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
-    cudaGetLastError();
-    return;
-  }
-  if (cap != cudaStreamCaptureStatusNone) return;
-  int pct = env_int("FMHA_STATIC_PERCENT", kStaticPercent);  // tuning knob, 0..100
-  if (pct < 0 || pct > 100) pct = kStaticPercent;
-  const int64_t rounds = steps * pct / 100 / warps;
-  if (warps >= 4096) return;  // 12-bit user count (one user per CTA, fewer CTAs than warps)
-  int dv = 0;
-  if (cudaGetDevice(&dv) != cudaSuccess) return;
-  // FMHA_SCHED_SLOTS (1..16) narrows the slot pool; tests use it to make
-  // concurrent launches contend for one word.
-  int nslots = env_int("FMHA_SCHED_SLOTS", kSchedSlots);
-  if (nslots < 1 || nslots > kSchedSlots) nslots = kSchedSlots;
-  const uint64_t seq = g_launch_seq[dv].fetch_add(1);
-  P.sched = dev.sched + (seq % (uint64_t)nslots) * kSchedSlotWords;
-  P.sched_tag = (uint32_t)(seq % 0xffffffu) + 1u;
-  P.sched_rounds = rounds;
-}
-
 fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev,
                          cudaStream_t stream, bool append = false) {
   KernelFn fn = append ? (d == 128 ? ldg_append_kernel_d128(smax, g)
@@ -318,7 +321,7 @@ fmha_status_t launch_ldg(Params P, int d, int smax, int g, const DeviceInfo& dev
   const int64_t need = (tiles + (int64_t)wpb * tpi - 1) / ((int64_t)wpb * tpi);
   int64_t grid = (int64_t)dev.sms * bps;
   if (grid > need) grid = need;
-  plan_schedule(P, dev, (tiles + tpi - 1) / tpi, grid * wpb, stream);
+  plan_schedule(P, dev, (tiles + tpi - 1) / tpi, grid * wpb, grid, stream);
   if (launch_overlapped(fn, (unsigned)grid, kLdgThreads, 0, stream, P) != cudaSuccess) {
     cudaGetLastError();
     return FMHA_ERR_CUDA;
@@ -471,8 +474,11 @@ fmha_status_t fmha_forward_varlen_variant(const void* Q, const void* K, const vo
     int64_t grid = (int64_t)dev.sms * bps;
     const int64_t need = ((int64_t)batch * qs + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
     if (grid > need) grid = need;
-    fn<<<(unsigned)grid, kLdgThreads, 0, cs>>>(P);
-    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+    if (launch_overlapped(fn, (unsigned)grid, kLdgThreads, 0, cs, P) != cudaSuccess) {
+      cudaGetLastError();
+      return FMHA_ERR_CUDA;
+    }
+    return FMHA_OK;
   }
   // Chunk ring: whole packed rows (or head groups) as chunks of a byte ring.
   VarlenFn cfn = head_dim == 128 ? varlen_chunk_kernel_d128(g) : varlen_chunk_kernel_d256(g);
@@ -496,8 +502,12 @@ fmha_status_t fmha_forward_varlen_variant(const void* Q, const void* K, const vo
   st = ensure_smem(reinterpret_cast<const void*>(cfn), dev.smem_optin);
   if (st != FMHA_OK) return st;
   const int grid = batch < dev.sms ? batch : dev.sms;
-  cfn<<<grid, 32 * (1 + ncw), P.ring_off + ring, cs>>>(P);
-  return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_CUDA;
+  if (launch_overlapped(cfn, (unsigned)grid, 32u * (1 + ncw), P.ring_off + ring, cs, P) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return FMHA_ERR_CUDA;
+  }
+  return FMHA_OK;
 }
 
 fmha_status_t fmha_forward_varlen(const void* Q, const void* K, const void* V, void* O,
