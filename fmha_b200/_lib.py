@@ -25,6 +25,7 @@ _vp, _i, _i64, _u64, _u32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctype
 SIGNATURES = {
     "fmha_forward": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "fmha_forward_variant": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "fmha_forward_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "fmha_forward_varlen": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp]),
     "fmha_forward_varlen_variant": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                                          ctypes.c_float, _i, _vp]),

@@ -1,8 +1,8 @@
 """Builds the native parts of fmha_b200 in-tree (no JIT cache):
 
 * ``fmha_b200/libfmha_b200.so`` -- the CUDA C-ABI library (include/fmha.h),
-  sm_100a only: decode_bulk.cu and decode_ldg.cu compiled once per head_dim,
-  plus fmha_api.cu;
+  sm_100a only: the decode_*.cu kernels compiled once per head_dim, plus
+  fmha_api.cu and fmha_noalloc.cu;
 * ``fmha_b200/bin/fmha_host`` -- the C++ benchmark/validation host linked
   against that library (when its source is present).
 
@@ -58,6 +58,7 @@ def _objects():
         objs.append((os.path.join(CSRC, src), os.path.join(BUILD, f"{stem}_d{d}.o"),
                      [f"-DFMHA_HEAD_DIM={d}"]))
     objs.append((os.path.join(CSRC, "fmha_api.cu"), os.path.join(BUILD, "fmha_api.o"), []))
+    objs.append((os.path.join(CSRC, "fmha_noalloc.cu"), os.path.join(BUILD, "fmha_noalloc.o"), []))
     return objs
 
 

@@ -140,6 +140,26 @@ fmha_status_t fmha_forward_append(const void* Q, void* K_cache, void* V_cache,
                                   int seqlen_kv, int cache_seqlen, int head_dim,
                                   fmha_stream_t stream);
 
+/*
+ * fmha_forward_noalloc -- fmha_forward for callers that cannot allocate
+ * device memory (an allocator hook that must not re-enter the allocator, a
+ * plug-in whose host owns every device allocation, a fixed memory budget).
+ * Same arguments, layouts, scale and status codes as fmha_forward; it always
+ * runs the ldg kernel family. Its only scratch, the kernel's work-schedule
+ * slot, is a 1152-byte static device array inside the library (held by every
+ * GPU that loads it until exit), so no call ever allocates. The first call
+ * on a device looks the array's address up and should come before any stream
+ * capture. All calls share the array: calls overlapping on the GPU race for
+ * it, and the one that finds it taken runs a static schedule (its output is
+ * still complete). Limits: at most 4095 CTAs per launch and
+ * batch * num_heads_kv <= 2^30, else FMHA_ERR_UNSUPPORTED.
+ * No counterpart in the reference (its host allocates everything itself).
+ */
+fmha_status_t fmha_forward_noalloc(const void* Q, const void* K, const void* V,
+                                   void* O, int batch, int num_heads_q,
+                                   int num_heads_kv, int seqlen_kv,
+                                   int head_dim, fmha_stream_t stream);
+
 /* Human-readable name of a status code (static storage). Reference
  * counterpart: the HIP_CHECK error text (fmha_host.cpp:26-35). */
 const char* fmha_status_string(fmha_status_t status);

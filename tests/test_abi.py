@@ -193,3 +193,25 @@ def test_seqlens_poisson_redraw_cap_ends_the_loop():
     st = fmha_b200.load().fmha_seqlens_poisson(4, 3, 42, 60.0, out.ctypes.data)
     assert st == _lib.FMHA_ERR_INVALID_ARG
     assert time.perf_counter() - t0 < 30
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(batch=1 << 26, num_heads_q=32, num_heads_kv=32), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(head_dim=64), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(seqlen_kv=17), _lib.FMHA_ERR_UNSUPPORTED),
+    (dict(q=40), _lib.FMHA_ERR_MISALIGNED),
+    (dict(o=0), _lib.FMHA_ERR_INVALID_ARG),
+    (dict(num_heads_q=24, num_heads_kv=16), _lib.FMHA_ERR_INVALID_ARG),
+])
+def test_noalloc_rejected_before_any_cuda_call(kw, status):
+    a = dict(BASE)
+    a.update(kw)
+    got = fmha_b200.load().fmha_forward_noalloc(a["q"], a["k"], a["v"], a["o"], a["batch"],
+                                                a["num_heads_q"], a["num_heads_kv"],
+                                                a["seqlen_kv"], a["head_dim"], None)
+    assert got == status
+
+
+def test_noalloc_empty_batch_is_a_noop():
+    assert fmha_b200.load().fmha_forward_noalloc(None, None, None, None, 0, 16, 16, 16, 128,
+                                                 None) == _lib.FMHA_OK
