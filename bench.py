@@ -617,15 +617,17 @@ def time_config(torch, fmha_b200, cfg, world, rank, args, variant, barrier, max_
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
     clk = None
-    if clocks and rank == 0:
-        # Too short a timed region for the sampler: keep the same kernel running
-        # (untimed) until ~1 s of load has been sampled.
+    if clocks:
+        # Too short a timed region for the sampler: every rank keeps the same
+        # kernel running (untimed) until ~1 s of load has been sampled, so each
+        # GPU's clock record is taken under load.
         t0 = time.perf_counter()
         while (time.perf_counter() - t0) * 1e3 < max(0.0, 1000.0 - ms * args.steps):
             for i in range(50):
                 call(i)
             torch.cuda.synchronize(dev)
-        clk = sampler.stop()
+        if rank == 0:
+            clk = sampler.stop()
     if fmha_b200.device_error() != 0:
         raise RuntimeError("device error word set during the timed region")
     ms_max = max_over_ranks(ms)

@@ -33,10 +33,11 @@ _i64, _int = ctypes.c_int64, ctypes.c_int
 
 
 def build(ref_dir: str | None = None) -> None:
-    """Compile the restatement, and the reference build when its sources exist."""
+    """Compile the restatement, and the reference build when its sources exist
+    (``ref_dir``, else $FMHA_REF_DIR; no built-in location)."""
     subprocess.check_call(["make", "-s", "-C", HERE, "all"])
-    ref_dir = ref_dir or os.environ.get("FMHA_REF_DIR", "/root/reference")
-    if os.path.isfile(os.path.join(ref_dir, "fmha_host.cpp")):
+    ref_dir = ref_dir or os.environ.get("FMHA_REF_DIR", "")
+    if ref_dir and os.path.isfile(os.path.join(ref_dir, "fmha_host.cpp")):
         subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF_DIR={ref_dir}"],
                               stderr=subprocess.DEVNULL)
 
