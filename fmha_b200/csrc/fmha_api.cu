@@ -199,37 +199,45 @@ cudaError_t launch_overlapped(void (*fn)(const Prm), unsigned grid, unsigned blo
 // Share of the steps dealt out statically; the rest is the dynamic tail.
 constexpr int kStaticPercent = 90;
 
-// Fills P's schedule fields for a persistent launch of `ctas` CTAs whose
-// `workers` (warps or producers) share `steps` steps: a slot and a fresh tag for eager launches, tag 0 (fully
-// static) while the stream is being captured into a CUDA graph (a captured
-// launch would replay one tag, and two replays must never share a tail) or
-// for grids beyond the 12-bit user count.
-void plan_schedule(Params& P, const DeviceInfo& dev, int64_t steps, int64_t workers,
-                   int64_t ctas, cudaStream_t stream) {
-  P.sched = nullptr;
-  P.sched_tag = 0;
-  P.sched_rounds = 0;
-  if (env_int("FMHA_STATIC_SCHEDULE", 0)) return;
+// Picks a schedule slot and a fresh tag for an eager launch of `ctas` CTAs;
+// false (run statically) while the stream is being captured into a CUDA
+// graph (a captured launch would replay one tag, and two replays must never
+// share a slot's counters), for grids beyond the 12-bit user count, or when
+// FMHA_STATIC_SCHEDULE is set.
+bool take_slot(const DeviceInfo& dev, int64_t ctas, cudaStream_t stream,
+               unsigned long long** slot, uint32_t* tag) {
+  if (env_int("FMHA_STATIC_SCHEDULE", 0)) return false;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
     cudaGetLastError();
-    return;
+    return false;
   }
-  if (cap != cudaStreamCaptureStatusNone) return;
-  int pct = env_int("FMHA_STATIC_PERCENT", kStaticPercent);  // tuning knob, 0..100
-  if (pct < 0 || pct > 100) pct = kStaticPercent;
-  const int64_t rounds = steps * pct / 100 / workers;
-  if (ctas >= 4096) return;  // 12-bit user count (one user per CTA)
+  if (cap != cudaStreamCaptureStatusNone) return false;
+  if (ctas >= 4096) return false;  // 12-bit user count (one user per CTA)
   int dv = 0;
-  if (cudaGetDevice(&dv) != cudaSuccess) return;
+  if (cudaGetDevice(&dv) != cudaSuccess) return false;
   // FMHA_SCHED_SLOTS (1..16) narrows the slot pool; tests use it to make
   // concurrent launches contend for one word.
   int nslots = env_int("FMHA_SCHED_SLOTS", kSchedSlots);
   if (nslots < 1 || nslots > kSchedSlots) nslots = kSchedSlots;
   const uint64_t seq = g_launch_seq[dv].fetch_add(1);
-  P.sched = dev.sched + (seq % (uint64_t)nslots) * kSchedSlotWords;
-  P.sched_tag = (uint32_t)(seq % 0xffffffu) + 1u;
-  P.sched_rounds = rounds;
+  *slot = dev.sched + (seq % (uint64_t)nslots) * kSchedSlotWords;
+  *tag = (uint32_t)(seq % 0xffffffu) + 1u;
+  return true;
+}
+
+// Fills P's schedule fields for a persistent launch of `ctas` CTAs whose
+// `workers` (warps) share `steps` steps: kStaticPercent of the steps static,
+// the rest claimed, or all static when take_slot declines.
+void plan_schedule(Params& P, const DeviceInfo& dev, int64_t steps, int64_t workers,
+                   int64_t ctas, cudaStream_t stream) {
+  P.sched = nullptr;
+  P.sched_tag = 0;
+  P.sched_rounds = 0;
+  if (!take_slot(dev, ctas, stream, &P.sched, &P.sched_tag)) return;
+  int pct = env_int("FMHA_STATIC_PERCENT", kStaticPercent);  // tuning knob, 0..100
+  if (pct < 0 || pct > 100) pct = kStaticPercent;
+  P.sched_rounds = steps * pct / 100 / workers;
 }
 
 fmha_status_t launch_bulk(Params P, int d, int smax, int g, int warps, const DeviceInfo& dev,
