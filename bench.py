@@ -306,6 +306,11 @@ def main():
                     help="varlen configs: rows cycle through these lengths, e.g. 3,4 (profiling)")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (small profiling cases only)")
+    ap.add_argument("--sweep-gb", type=float, default=0.0,
+                    help="--sweep: shrink each config's batch to about this many GB per call "
+                         "(never below 3x L2; small cases for ncu captures)")
+    ap.add_argument("--traffic-from", default="",
+                    help="write profiles/ncu_traffic.json from an ncu CSV of a --sweep-gb run")
     ap.add_argument("--sweep", action="store_true",
                     help="device-time lines for every config and variant (no e2e/cpu)")
     ap.add_argument("--sweep-configs", default="",
@@ -318,6 +323,8 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
 
+    if args.traffic_from:
+        return write_traffic_table(args)
     if args.impl == "reference":
         return run_reference_arm(args, args.config, CONFIGS[args.config])
 
@@ -357,6 +364,8 @@ def main():
             cfg_n = CONFIGS[name]
             if args.batch > 0:
                 cfg_n = (args.batch,) + tuple(cfg_n[1:])
+            elif args.sweep_gb > 0:
+                cfg_n = (small_batch(name, args.sweep_gb),) + tuple(cfg_n[1:])
             for var, warps in trials:
                 if warps is not None:
                     os.environ["FMHA_BULK_WARPS"] = str(warps)
@@ -435,6 +444,67 @@ def main():
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
+    return 0
+
+
+def row_bytes(name):
+    """Algorithmic bytes of one batch row of a config (varlen: at the mean
+    Poisson(4) length in [2, 16], 4.35)."""
+    _, hq, hkv, s, d = CONFIGS[name]
+    if name in VARLEN:
+        return 4 * hq * d + 4 * 4.35 * hkv * d
+    return algo_bytes(1, hq, hkv, s, d)
+
+
+def small_batch(name, gb):
+    """A batch for a small profiling case of `name`: about `gb` GB per call,
+    at least 3x L2 of traffic, at most the config's own batch."""
+    b_all = CONFIGS[name][0]
+    want = max(gb * 1e9, 3 * L2_BYTES) / row_bytes(name)
+    return int(min(b_all, max(1, math.ceil(want))))
+
+
+def write_traffic_table(args):
+    """profiles/ncu_traffic.json from the ncu CSV of
+    `bench.py --sweep --sweep-auto --sweep-gb G --steps K --warmup W` run under
+    `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum`:
+    per config, the last captured launch's DRAM bytes, scaled from the small
+    batch to the config's full batch by rows (read traffic grows in proportion
+    to the rows processed)."""
+    import csv
+    names = [x for x in args.sweep_configs.split(",") if x] or sorted(CONFIGS)
+    per = args.warmup + args.steps
+    rows = {}
+    with open(args.traffic_from) as f:
+        lines = [ln for ln in f if ln.startswith('"')]
+    for r in csv.DictReader(lines):
+        if "decode" not in r.get("Kernel Name", ""):
+            continue
+        key = int(r["ID"])
+        e = rows.setdefault(key, {"kernel": r["Kernel Name"].split("(")[0]})
+        e[r["Metric Name"]] = float(r["Metric Value"].replace(",", ""))
+        e[r["Metric Name"] + " unit"] = r["Metric Unit"]
+    launches = [rows[k] for k in sorted(rows)]
+    if len(launches) != per * len(names):
+        raise SystemExit(f"{len(launches)} decode launches in the CSV, expected "
+                         f"{per} x {len(names)} configs")
+    scale_unit = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    table = {"_note": "DRAM bytes (read + write) per full-size launch of each config's "
+                      "dominant kernel: ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                      f"small case (about {args.sweep_gb} GB per call, >= 3x L2), scaled to the "
+                      "config's batch by rows processed"}
+    for i, name in enumerate(names):
+        e = launches[(i + 1) * per - 1]
+        rd = e["dram__bytes_read.sum"] * scale_unit[e["dram__bytes_read.sum unit"]]
+        wr = e["dram__bytes_write.sum"] * scale_unit[e["dram__bytes_write.sum unit"]]
+        b_small = small_batch(name, args.sweep_gb)
+        b_all = CONFIGS[name][0]
+        table[name] = round((rd + wr) * b_all / b_small)
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    with open(p, "w") as f:
+        json.dump(table, f, indent=1, sort_keys=True)
+        f.write("\n")
+    print(f"wrote {len(table)} configs to {p}")
     return 0
 
 
