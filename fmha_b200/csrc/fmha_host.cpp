@@ -19,8 +19,10 @@
 //
 // Usage: fmha_host [config_index] [--all] [--gpus N] [--iters N] [--warmups N]
 //                  [--seqlen S] [--seed S] [--variant auto|bulk|ldg]
-//                  [--validate-rows N] [--json] [--varlen]
+//                  [--validate-rows N] [--json] [--varlen] [--traffic FILE]
 //
+// --traffic profiles/ncu_traffic.json adds the DRAM bytes ncu measured for the
+// config (scaled to its batch) and the bandwidth they give.
 // --varlen runs the reference's own benchmark exactly: packed K/V
 // [sum S_b, Hkv, D] with cu_seqlens_kv and Poisson(4) lengths in [2, 16]
 // from mt19937(42) (fmha_host.cpp:58-82), through fmha_forward_varlen.
@@ -93,6 +95,7 @@ struct Options {
   int validate_rows = 64;
   bool json = false;
   bool varlen = false;  // the reference's packed layout and Poisson(4) seqlens
+  std::string traffic;  // measured-traffic table (profiles/ncu_traffic.json), optional
 };
 
 // ------------------------------------------------------------ host generator
@@ -382,6 +385,37 @@ void run_shard(int gpu, const Config& cfg, const Options& o, int64_t row0, int64
   cleanup();
 }
 
+// DRAM bytes per call of this config from a measured-traffic table: a JSON
+// object of config name -> bytes per full-size (batch 30720) launch, as
+// bench.py --traffic-from writes it (ncu dram__bytes_read.sum +
+// dram__bytes_write.sum). Scaled to `batch` rows; < 0 when absent.
+double measured_traffic(const std::string& path, int hq, int hkv, int s, int d, bool varlen,
+                        int batch) {
+  if (path.empty()) return -1.0;
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) return -1.0;
+  std::string txt;
+  char buf[4096];
+  size_t n;
+  while ((n = std::fread(buf, 1, sizeof(buf), f)) > 0) txt.append(buf, n);
+  std::fclose(f);
+  char key[96];
+  if (varlen && hq == hkv)
+    std::snprintf(key, sizeof(key), "\"varlen_h%d_d%d\"", hq, d);
+  else if (varlen)
+    std::snprintf(key, sizeof(key), "\"varlen_gqa_%d_%d_d%d\"", hq, hkv, d);
+  else if (hq == hkv)
+    std::snprintf(key, sizeof(key), "\"h%d_d%d_s%d\"", hq, d, s);
+  else
+    std::snprintf(key, sizeof(key), "\"gqa_%d_%d_d%d_s%d\"", hq, hkv, d, s);
+  const size_t at = txt.find(key);
+  if (at == std::string::npos) return -1.0;
+  const size_t colon = txt.find(':', at);
+  if (colon == std::string::npos) return -1.0;
+  const double full = std::strtod(txt.c_str() + colon + 1, nullptr);
+  return full > 0 ? full * batch / 30720.0 : -1.0;
+}
+
 bool run_config(int idx, const Options& o) {
   const Config& cfg = kConfigs[idx];
   const int hq = cfg.num_heads_q, hkv = cfg.num_heads_kv, d = cfg.head_dim, s = o.seqlen;
@@ -442,6 +476,8 @@ bool run_config(int idx, const Options& o) {
   const int threads = omp_get_max_threads();
   const bool ok = bad == 0 && dev_err == 0 && failed.empty();
   const bool any = ms > 0;  // at least one shard completed
+  const double traffic = measured_traffic(o.traffic, hq, hkv, s, d, o.varlen, cfg.batch);
+  const double ncu_gbs = traffic > 0 && ms > 0 ? traffic * done_frac / (ms * 1e-3) / 1e9 : -1.0;
   if (o.json) {
     std::printf(
         "{\"config\": %d, \"note\": \"%s\", \"batch\": %d, \"num_heads_q\": %d, "
@@ -449,11 +485,11 @@ bool run_config(int idx, const Options& o) {
         "\"us_per_call\": %.3f, \"gbs\": %.1f, \"tflops\": %.3f, \"rows_checked\": %lld, "
         "\"bad\": %lld, \"max_abs_err\": %.3e, \"max_rel_err\": %.3e, \"cpu_ms_per_row\": %.4f, "
         "\"cpu_threads\": %d, \"device_error\": %d, \"varlen\": %s, \"failed_shards\": \"%s\", "
-        "\"passed\": %s}\n",
+        "\"ncu_dram_bytes\": %.0f, \"ncu_gbs\": %.1f, \"passed\": %s}\n",
         idx, cfg.note, cfg.batch, hq, hkv, o.varlen ? -1 : s, d, n, ms * 1e3, gbs,
         any ? flops / (ms * 1e-3) / 1e12 : 0.0,
         (long long)checked, (long long)bad, max_abs, max_rel, cpu_ms_per_row, threads, dev_err,
-        o.varlen ? "true" : "false", failed.c_str(), ok ? "true" : "false");
+        o.varlen ? "true" : "false", failed.c_str(), traffic, ncu_gbs, ok ? "true" : "false");
   } else {
     std::printf("\n=== Configuration %d (%s) ===\n", idx, cfg.note);
     if (o.varlen) {
@@ -472,6 +508,9 @@ bool run_config(int idx, const Options& o) {
     std::printf("Performance:   %.3f TFLOPS\n", flops / (ms * 1e-3) / 1e12);
     std::printf("Per-head latency: %.6f us\n", ms * 1e3 / (b * hq));
     std::printf("Memory bandwidth: %.1f GB/s (algorithmic bytes)\n", gbs);
+    if (ncu_gbs > 0)
+      std::printf("Memory bandwidth: %.1f GB/s (DRAM bytes measured by ncu, %s)\n", ncu_gbs,
+                  o.traffic.c_str());
     std::printf("Validation: %lld rows on the CPU (%d OpenMP threads, %.3f ms/row): %s, "
                 "max abs err %.3e, max rel err %.3e\n",
                 (long long)checked, threads, cpu_ms_per_row, ok ? "passed" : "FAILED", max_abs,
@@ -484,7 +523,7 @@ void usage() {
   std::fprintf(stderr,
                "usage: fmha_host [config_index 0..%d] [--all] [--gpus N] [--iters N] "
                "[--warmups N] [--seqlen 1..16] [--seed S] [--variant auto|bulk|ldg] "
-               "[--validate-rows N] [--json] [--varlen]\n",
+               "[--validate-rows N] [--json] [--varlen] [--traffic ncu_traffic.json]\n",
                kNumConfigs - 1);
 }
 
@@ -511,6 +550,7 @@ int main(int argc, char** argv) {
     else if (a == "--validate-rows") o.validate_rows = std::atoi(next("--validate-rows"));
     else if (a == "--json") o.json = true;
     else if (a == "--varlen") o.varlen = true;
+    else if (a == "--traffic") o.traffic = next("--traffic");
     else if (a == "--variant") {
       std::string v = next("--variant");
       o.variant = v == "bulk" ? FMHA_VARIANT_BULK : v == "ldg" ? FMHA_VARIANT_LDG

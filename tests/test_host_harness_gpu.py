@@ -52,3 +52,15 @@ def test_fmha_host_stuck_shard_returns_without_blocking(cuda):
                        timeout=300, env=env)
     assert r.returncode != 0
     assert "shard on GPU 0 failed: timed out" in r.stderr
+
+
+def test_fmha_host_reports_measured_traffic(cuda):
+    """--traffic reads the committed ncu table and adds the DRAM bytes ncu
+    measured for the config (scaled to its batch) and the bandwidth they give."""
+    table = os.path.join(os.path.dirname(BIN), "..", "..", "profiles", "ncu_traffic.json")
+    r = subprocess.run([BIN, "4", "--json", "--iters", "3", "--validate-rows", "8", "--traffic",
+                        table], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["ncu_dram_bytes"] > 0.9 * 17.11e9
+    assert 0.8 * line["gbs"] < line["ncu_gbs"] <= 1.01 * line["gbs"]
