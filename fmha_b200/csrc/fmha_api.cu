@@ -492,7 +492,10 @@ fmha_status_t fmha_forward_varlen_variant(const void* Q, const void* K, const vo
   VarlenFn cfn = head_dim == 128 ? varlen_chunk_kernel_d128(g) : varlen_chunk_kernel_d256(g);
   if (!cfn) return FMHA_ERR_UNSUPPORTED;
   P.wait_timeout_ns = kWaitTimeoutNs;
-  int ncw = env_int("FMHA_VARLEN_WARPS", 16);
+  // Consumer warps: 12 at D=256, 16 at D=128 (in-process A/B on the
+  // reference's table: 12 beat 16 by 1.5-3 % on every D=256 shape, and lost
+  // 5-8 % at D=128).
+  int ncw = env_int("FMHA_VARLEN_WARPS", head_dim == 256 ? 12 : 16);
   if (ncw < 1) ncw = 1;
   if (ncw > kBulkMaxThreads / 32 - 1) ncw = kBulkMaxThreads / 32 - 1;
   P.sc_off = kVarlenChunkHdr;
