@@ -126,15 +126,17 @@ int smax_for(int s) {
 
 int rows_per_access(int d) { return 256 / d; }
 
-// Per-shape default: kernel family and bulk consumer-warp count, from a B200
-// sweep (bench.py --sweep, batch 30720, 100 calls per point). The ldg family
-// wins where one unit already fills a 16-row tile with 512-byte rows
-// (D=256, S=16, one query head per kv head) and for D=128, S=1; elsewhere the
-// bulk ring wins, with ~10 consumer warps for 8-16 row units (leaving ring
-// stages for copies in flight) and 16 for short units (more tiles per stage).
-// With 4 or 8 query heads per kv head the choice flips for D=256 short rows
-// (ldg) and D=128 long rows (16 warps). FMHA_VARIANT (1 bulk, 2 ldg) and
-// FMHA_BULK_WARPS override the table.
+// Per-shape default: kernel family and bulk consumer-warp count, from B200
+// sweeps (bench.py --sweep, batch 30720; last re-swept after the packed-FMA
+// P.V and the ldg kernel's dynamic tail). The ldg family wins where one unit
+// already fills a 16-row tile with 512-byte rows (D=256, S=16, one query head
+// per kv head), for seqlen 1 with one or two query heads per kv head, and for
+// D=256, S<=2 with two; elsewhere the bulk ring wins, with ~10 consumer warps
+// for 9-16 row units (leaving ring stages for copies in flight), 16 for
+// shorter ones and for D=256 S 5-8. With 4 or 8 query heads per kv head the
+// choice flips for D=256 short rows (ldg, except 4 heads at S=1 or S 3-4:
+// bulk with 8 warps) and D=128 long rows (16 warps). FMHA_VARIANT (1 bulk,
+// 2 ldg) and FMHA_BULK_WARPS override the table.
 struct Choice {
   int variant;
   int warps;
@@ -144,16 +146,17 @@ Choice auto_choice(int d, int smax, int g) {
   static const int forced = env_int("FMHA_VARIANT", 0);
   Choice c{FMHA_VARIANT_BULK, 16};
   if (g >= 4) {
-    // 4 or 8 query heads per kv head (measured separately; S >= 5 runs the
-    // bulk kernel's tensor-core tile).
+    // 4 or 8 query heads per kv head (S >= 5 runs the bulk kernel's
+    // tensor-core tile).
     if (d == 128) c = smax == 1 ? Choice{FMHA_VARIANT_LDG, 0} : Choice{FMHA_VARIANT_BULK, 16};
     else if (smax >= 8) c = {FMHA_VARIANT_BULK, 8};
-    else if (g == 4 && smax == 1) c = {FMHA_VARIANT_BULK, 8};
+    else if (g == 4 && (smax == 1 || smax == 4)) c = {FMHA_VARIANT_BULK, 8};
     else c = {FMHA_VARIANT_LDG, 0};
   } else if (d == 256 && smax == 16 && g == 1) c = {FMHA_VARIANT_LDG, 0};
-  else if (d == 128 && smax == 1 && g == 1) c = {FMHA_VARIANT_LDG, 0};
+  else if (smax == 1) c = {FMHA_VARIANT_LDG, 0};
+  else if (d == 256 && smax == 2 && g == 2) c = {FMHA_VARIANT_LDG, 0};
+  else if (d == 256 && smax == 8) c = {FMHA_VARIANT_BULK, 16};
   else if (smax >= 8) c = {FMHA_VARIANT_BULK, 10};
-  else if (d == 128 && smax == 4) c = {FMHA_VARIANT_BULK, 8};
   if (forced == FMHA_VARIANT_BULK || forced == FMHA_VARIANT_LDG) c.variant = forced;
   if (c.warps == 0) c.warps = 10;
   return c;
