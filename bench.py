@@ -15,10 +15,18 @@ own formula (fmha_host.cpp:428-431). ms_per_step is the matching us/call.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config NAME] [--variant auto|bulk|ldg] [--sweep]
 
+After the timed region each rank checks every row of its output against the
+CPU oracle (`parity`), reports every rank's device time (`per_rank_ms`), and,
+with N > 1, all-gathers the sharded O over NCCL and checks it (`gather`).
+
 --impl reference times the reference's own CPU implementation of the path
 (oracle/_ref: the reference's do_validation compiled from its sources; the
-oracle port if that build is absent) on the host cores, on a bounded sample of
-the same workload; under torchrun only rank 0 runs it.
+oracle port if that build is absent) on the host cores, on the full batch
+every step; under torchrun only rank 0 runs it.
+
+--sweep [--sweep-auto] [--sweep-gb G] prints device-time lines for every
+config (small cases of about G GB for ncu captures); --traffic-from CSV turns
+the ncu CSV of such a run into profiles/ncu_traffic.json.
 """
 from __future__ import annotations
 
