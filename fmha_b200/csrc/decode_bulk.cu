@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kBulkMaxThreads, 1) decode_bulk_kernel(const P
           if (u >= uv) break;
           const int ju = j * T::NU + u;
           const uint32_t k0 = sbase + (uint32_t)(ju * s_len) * (D * 2);
-          attend_unit_mma<D, G>(k0, k0 + P.v_off, sbase + P.q_off + (uint32_t)ju * (G * D * 2),
+          attend_unit_mma<D, G, SMAX == 8>(k0, k0 + P.v_off, sbase + P.q_off + (uint32_t)ju * (G * D * 2),
                                 s_len, P.scale_log2, P.O + (tile_u0 + u) * (G * D), lane);
         }
       } else {

@@ -756,7 +756,9 @@ __device__ __forceinline__ uint32_t half16(const uint4 v, int i) {  // element i
   return (i & 1) ? (w >> 16) : (w & 0xffffu);
 }
 
-template <int D, int G>
+// HALF: the unit has at most 8 rows (SMAX = 8), so K rows 8-15 -- the next
+// unit's, masked anyway -- are neither loaded nor multiplied.
+template <int D, int G, bool HALF = false>
 __device__ __forceinline__ void attend_unit_mma(uint32_t kbase, uint32_t vbase, uint32_t qbase,
                                                 int s_len, float scale_log2, uint16_t* O,
                                                 int lane) {
@@ -769,11 +771,13 @@ __device__ __forceinline__ void attend_unit_mma(uint32_t kbase, uint32_t vbase, 
     const uint32_t col = (uint32_t)(32 * j + 8 * t) * 2;
     const uint4 qa = g < G ? lds128(qbase + (uint32_t)g * (D * 2) + col) : z;
     const uint4 k0 = lds128(kbase + (uint32_t)g * (D * 2) + col);
-    const uint4 k1 = lds128(kbase + (uint32_t)(g + 8) * (D * 2) + col);
     mma_16816(c0, qa.x, qa.y, k0.x, k0.y);
-    mma_16816(c1, qa.x, qa.y, k1.x, k1.y);
     mma_16816(c0, qa.z, qa.w, k0.z, k0.w);
-    mma_16816(c1, qa.z, qa.w, k1.z, k1.w);
+    if constexpr (!HALF) {
+      const uint4 k1 = lds128(kbase + (uint32_t)(g + 8) * (D * 2) + col);
+      mma_16816(c1, qa.x, qa.y, k1.x, k1.y);
+      mma_16816(c1, qa.z, qa.w, k1.z, k1.w);
+    }
   }
   // Scores of row g: s = 2t, 2t+1 (c0), 8+2t, 9+2t (c1).
   float x[4] = {c0[0], c0[1], c1[0], c1[1]};
